@@ -1,0 +1,68 @@
+/* sh_ops_cuda.h -- extensions of libsh_ops_cuda.so beyond the reference header (runtime/sh_ops.h).
+ *
+ * They have no counterpart in the reference: they expose what a GPU backend needs and a RISC-V cluster did not
+ * (caller-owned device memory, streams, asynchronous error state) and the fused / batched forms of the hot-path
+ * ops that the encoder driver uses (GEMM epilogues, residual + LayerNorm, attention over a batch of sequences).
+ * All pointers are device pointers passed as uint64_t, sizes and leading dimensions are in elements, like the
+ * reference ABI.
+ */
+#ifndef SH_OPS_CUDA_H
+#define SH_OPS_CUDA_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- runtime ------------------------------------------------------------------------------------------------
+ * Bind caller-owned device memory (e.g. a torch tensor's data_ptr) as the HBM arena of the current device;
+ * the library never frees it. Returns 0, or -1 when base is NULL / not 256-byte aligned. */
+int      sh_cuda_set_arena(void *base, size_t bytes);
+void    *sh_cuda_arena_base(void);
+size_t   sh_cuda_arena_bytes(void);
+/* All ops of the calling thread's current device are enqueued on this stream (a cudaStream_t; NULL = the
+ * legacy default stream). */
+int      sh_cuda_set_stream(void *stream);
+void    *sh_cuda_get_stream(void);
+int      sh_cuda_synchronize(void);                 /* stream sync; returns the cudaError_t code */
+int      sh_cuda_last_error(void);                  /* first error recorded since the previous call, then cleared */
+const char *sh_cuda_last_error_string(void);        /* text of that error ("" when none) */
+int      sh_cuda_device_error(void);                /* syncs, returns and clears the kernels' error word (1 = a
+                                                       bounded wait gave up) */
+int      sh_cuda_num_sms(void);
+float    sh_cuda_timer_last_ms(void);               /* the period the last sh_timer_end printed */
+uint32_t sh_cuda_abi_version(void);                 /* 1 */
+
+/* ---- GEMM with fused epilogue ---------------------------------------------------------------------------------
+ * Z[M,N] = epi(X[M,K] . W[K,N]) with fp32 accumulation, fp16 out. `flags`:
+ *   SH_EPI_ACCUMULATE  t = acc + Z_old           (sh_gemm_cfg.accumulate)
+ *   SH_EPI_BIAS        t = t + bias[col]         (bias: 1 x N fp16)
+ *   SH_EPI_GELU        t = gelu_tanh(t)          (after the bias)
+ *   SH_EPI_RESIDUAL    t = t + R[row, col]       (R: M x N fp16, leading dim ldr)
+ *   SH_GEMM_SIMT       use the CUDA-core fallback kernel (tests)
+ * splits: 0 = library choice of split-K, 1 = none, n = K split n ways (partials reduced in a fixed order).
+ * Returns 0 or -1 (reason printed). */
+#define SH_EPI_ACCUMULATE 0x1u
+#define SH_EPI_BIAS       0x2u
+#define SH_EPI_GELU       0x4u
+#define SH_EPI_RESIDUAL   0x8u
+#define SH_GEMM_SIMT      0x100u
+int sh_cuda_gemm(uint64_t x, uint64_t w, uint64_t z, uint32_t M, uint32_t N, uint32_t K, uint32_t ldx, uint32_t ldw,
+                 uint32_t ldz, uint64_t bias, uint64_t residual, uint32_t ldr, uint32_t flags, uint32_t splits);
+
+/* ---- fused residual add + LayerNorm ---------------------------------------------------------------------------
+ * h = a + b (stored, fp16), y = layernorm(h) * gamma + beta, both rows x cols with leading dim ld. */
+void sh_cuda_add_layernorm(uint64_t h, uint64_t y, uint64_t a, uint64_t b, uint64_t gamma, uint64_t beta,
+                           uint32_t rows, uint32_t cols, uint32_t ld, float eps);
+
+/* ---- attention over a batch of sequences ------------------------------------------------------------------------
+ * B sequences of S rows stacked along the rows of q/k/v/o (sequence b = rows [b S, (b+1) S)); otherwise
+ * sh_attention. Returns 0 or -1. */
+int sh_cuda_attention_batched(uint64_t q, uint64_t k, uint64_t v, uint64_t o, uint32_t S, uint32_t D, uint32_t H,
+                              uint32_t ldq, uint32_t ldk, uint32_t ldv, uint32_t ldo, float scale, uint32_t B);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SH_OPS_CUDA_H */

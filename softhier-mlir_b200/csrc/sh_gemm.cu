@@ -1,0 +1,598 @@
+// GEMM of the operator library: Z[M,N] (+)= X[M,K] . W[K,N], fp16 in, fp32 accumulate, fp16 out
+// (reference: runtime/sh_gemm.inc.c:17-117 sh_cfg_fill / sh_gemm_l1_bytes / sh_gemm, :127-189 sh_gemm_mesh,
+// :192-344 sh_gemm_xmcast_ex; declared at runtime/sh_ops.h:54-88).
+//
+// The reference streams tm x tk / tk x tn tiles into TCDM and accumulates on RedMulE. Here one persistent CTA per
+// SM runs a warp-specialised tcgen05 pipeline:
+//   warp 0    TMA producer: X tile [128 x 64] (K-major) and W tile [64 x BN] (N-major, i.e. W as stored) per
+//             stage into a multi-stage ring of 128-byte-swizzled shared memory, completion on mbarriers;
+//   warp 1    MMA issuer: one thread issues tcgen05.mma (M=128, N=BN, K=16) into one of two TMEM accumulators
+//             and tcgen05.commit frees each stage / publishes each finished accumulator;
+//   warps 2-5 epilogue: tcgen05.ld the accumulator (each warp owns its 32-lane quarter = 32 rows), apply the
+//             fused epilogue (accumulate / bias / GELU / residual) and store fp16; the second accumulator lets the
+//             next tile's MMAs run meanwhile.
+// Split-K ("K-accumulation" across CTAs) writes fp32 partial tiles to a workspace; the last CTA to finish a tile
+// (arrival counter) sums the partials in split order and runs the epilogue, then resets the counter.
+// Every mbarrier wait is bounded (SH_SPIN_CYCLES): on a timeout the CTA raises the device error word, skips its
+// remaining work, waits for its outstanding TMA loads and frees its tensor memory.
+// Shapes the TMA path cannot address (16-byte alignment of base or leading dimension) use a CUDA-core kernel.
+#include <string.h>
+
+#include "sh_internal.cuh"
+
+namespace {
+
+constexpr int BM = 128;
+constexpr int BK = 64;
+constexpr int kThreads = 192;
+
+template <int BN>
+struct TileCfg {
+    static constexpr int kStages = BN == 256 ? 4 : (BN == 128 ? 6 : 8);
+    static constexpr uint32_t kABytes = BM * BK * 2;
+    static constexpr uint32_t kBBytes = BK * BN * 2;
+    static constexpr uint32_t kStageBytes = kABytes + kBBytes;
+    static constexpr uint32_t kTmemCols = 2 * BN;
+    static constexpr uint32_t kSmem = kStages * kStageBytes + 1024 + 256;
+};
+
+struct GemmArgs {
+    __half *z;
+    const __half *bias;
+    const __half *resid;
+    uint32_t M, N, K, ldz, ldr, flags;
+    uint32_t tiles_n, num_tiles, k_blocks, splits, kb_per_split;
+    uint32_t vec;   // epilogue may use 16-byte accesses on z / bias / resid
+    float *ws;
+    uint32_t *counters;
+    int *err;
+};
+
+// Barrier of the four epilogue warps on an mbarrier (count 4), so that it is bounded like every other wait.
+__device__ __forceinline__ bool epi_sync(uint64_t *bar, uint32_t &phase, volatile int *abort, int *err) {
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) mbar_arrive(bar);
+    const bool ok = mbar_wait(bar, phase, abort, err);
+    phase ^= 1u;
+    __syncwarp();
+    return ok;
+}
+
+// Bounded wait that ignores the abort flag: used to drain outstanding asynchronous work before exit.
+__device__ __forceinline__ void drain_wait(uint64_t *bar, uint32_t parity) {
+    const long long t0 = clock64();
+    while (!mbar_try_wait(bar, parity))
+        if ((unsigned long long)(clock64() - t0) > SH_SPIN_CYCLES) break;
+}
+
+// fused epilogue of 8 consecutive columns of one row (values in v, fp32)
+__device__ __forceinline__ void epilogue8(const GemmArgs &a, uint32_t row, uint32_t col, float (&v)[8]) {
+    if (row >= a.M || col >= a.N) return;
+    const uint32_t f = a.flags;
+    __half *zp = a.z + (size_t)row * a.ldz + col;
+    if (a.vec && col + 8 <= a.N) {
+        if (f & SH_EPI_ACCUMULATE) {
+            uint4 raw = *reinterpret_cast<const uint4 *>(zp);
+            const __half2 *h = reinterpret_cast<const __half2 *>(&raw);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                float2 t = __half22float2(h[i]);
+                v[2 * i] += t.x;
+                v[2 * i + 1] += t.y;
+            }
+        }
+        if (f & SH_EPI_BIAS) {
+            uint4 raw = __ldg(reinterpret_cast<const uint4 *>(a.bias + col));
+            const __half2 *h = reinterpret_cast<const __half2 *>(&raw);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                float2 t = __half22float2(h[i]);
+                v[2 * i] += t.x;
+                v[2 * i + 1] += t.y;
+            }
+        }
+        if (f & SH_EPI_GELU) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] = gelu_tanh(v[i]);
+        }
+        if (f & SH_EPI_RESIDUAL) {
+            uint4 raw = *reinterpret_cast<const uint4 *>(a.resid + (size_t)row * a.ldr + col);
+            const __half2 *h = reinterpret_cast<const __half2 *>(&raw);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                float2 t = __half22float2(h[i]);
+                v[2 * i] += t.x;
+                v[2 * i + 1] += t.y;
+            }
+        }
+        uint4 out;
+        __half2 *o = reinterpret_cast<__half2 *>(&out);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) o[i] = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+        *reinterpret_cast<uint4 *>(zp) = out;
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const uint32_t c = col + i;
+            if (c >= a.N) break;
+            float t = v[i];
+            if (f & SH_EPI_ACCUMULATE) t += __half2float(zp[i]);
+            if (f & SH_EPI_BIAS) t += __half2float(a.bias[c]);
+            if (f & SH_EPI_GELU) t = gelu_tanh(t);
+            if (f & SH_EPI_RESIDUAL) t += __half2float(a.resid[(size_t)row * a.ldr + c]);
+            zp[i] = __float2half_rn(t);
+        }
+    }
+}
+
+template <int BN>
+__global__ void __launch_bounds__(kThreads, 1)
+    k_gemm_tc(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w, GemmArgs a) {
+    using C = TileCfg<BN>;
+    constexpr int S = C::kStages;
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
+    uint8_t *smem = smem_raw + pad;
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + S * C::kStageBytes);
+    uint64_t *empty = full + S;
+    uint64_t *tfull = empty + S;    // [2] accumulator ready for the epilogue
+    uint64_t *tempty = tfull + 2;   // [2] accumulator drained by the epilogue
+    uint64_t *esync = tempty + 2;   // epilogue-group barrier (split-K arrival protocol)
+    uint64_t *mdone = esync + 1;    // every issued MMA has completed (exit path)
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mdone + 1);
+    volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
+    volatile uint32_t *last_flag = reinterpret_cast<volatile uint32_t *>(tmem_slot + 2);
+
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&tfull[i], 1);
+            mbar_init(&tempty[i], 4);
+        }
+        mbar_init(esync, 4);
+        mbar_init(mdone, 1);
+        *abort = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, C::kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    const uint32_t total_units = a.num_tiles * a.splits;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---------------- TMA producer ----------------
+            prefetch_tmap(&map_x);
+            prefetch_tmap(&map_w);
+            uint32_t stage = 0, phase = 0;
+            uint32_t armed[S];
+            for (int s = 0; s < S; ++s) armed[s] = 2;   // 2 = never armed
+            bool ok = true;
+            for (uint32_t u = blockIdx.x; ok && u < total_units; u += gridDim.x) {
+                const uint32_t tile = u / a.splits, split = u - tile * a.splits;
+                const uint32_t tm = tile / a.tiles_n, tn = tile - tm * a.tiles_n;
+                const uint32_t kb0 = split * a.kb_per_split;
+                const uint32_t kb1 = min(a.k_blocks, kb0 + a.kb_per_split);
+                for (uint32_t kb = kb0; kb < kb1; ++kb) {
+                    if (!mbar_wait(&empty[stage], phase ^ 1u, abort, a.err)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t *sa = smem + stage * C::kStageBytes;
+                    uint8_t *sb = sa + C::kABytes;
+                    mbar_arrive_expect_tx(&full[stage], C::kStageBytes);
+                    armed[stage] = phase;
+                    tma_load_2d(sa, &map_x, &full[stage], (int32_t)(kb * BK), (int32_t)(tm * BM));
+#pragma unroll
+                    for (int c = 0; c < BN / 64; ++c)
+                        tma_load_2d(sb + c * (BK * 128), &map_w, &full[stage], (int32_t)(tn * BN + c * 64),
+                                    (int32_t)(kb * BK));
+                    if (++stage == S) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            // drain: every armed stage's last transaction must have landed before the CTA may exit
+            for (int s = 0; s < S; ++s)
+                if (armed[s] != 2) drain_wait(&full[s], armed[s]);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ---------------- MMA issuer ----------------
+            constexpr uint32_t idesc = umma_idesc_f16(BM, BN, 0, 1);
+            uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
+            bool ok = true;
+            for (uint32_t u = blockIdx.x; ok && u < total_units; u += gridDim.x) {
+                const uint32_t tile = u / a.splits, split = u - tile * a.splits;
+                (void)tile;
+                const uint32_t kb0 = split * a.kb_per_split;
+                const uint32_t kb1 = min(a.k_blocks, kb0 + a.kb_per_split);
+                if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort, a.err)) break;
+                tc_fence_after();
+                const uint32_t d = tmem_base + acc * BN;
+                for (uint32_t kb = kb0; kb < kb1; ++kb) {
+                    if (!mbar_wait(&full[stage], phase, abort, a.err)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t sa = smem_u32(smem + stage * C::kStageBytes);
+                    const uint32_t sb = sa + C::kABytes;
+#pragma unroll
+                    for (int j = 0; j < BK / 16; ++j) {
+                        const uint64_t ad = sw128_desc(sa + j * 32, 16, 1024);
+                        const uint64_t bd = sw128_desc(sb + j * 2048, BK * 128, 1024);
+                        umma_f16_ss(d, ad, bd, idesc, (kb > kb0 || j > 0) ? 1u : 0u);
+                    }
+                    umma_commit(&empty[stage]);
+                    if (++stage == S) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                umma_commit(&tfull[acc]);
+                acc ^= 1u;
+                if (acc == 0) acc_phase ^= 1u;
+            }
+            // exit path: tensor memory may only be freed once every issued MMA has completed
+            umma_commit(mdone);
+            drain_wait(mdone, 0);
+        }
+    } else {
+        // ---------------- epilogue (warps 2..5) ----------------
+        const uint32_t quarter = warp & 3u;   // TMEM lanes [32 quarter, 32 quarter + 32)
+        const uint32_t row_in_tile = quarter * 32 + lane;
+        uint32_t acc = 0, acc_phase = 0, es_phase = 0;
+        for (uint32_t u = blockIdx.x; u < total_units; u += gridDim.x) {
+            const uint32_t tile = u / a.splits, split = u - tile * a.splits;
+            const uint32_t tm = tile / a.tiles_n, tn = tile - tm * a.tiles_n;
+            if (!mbar_wait(&tfull[acc], acc_phase, abort, a.err)) break;
+            tc_fence_after();
+            const uint32_t row = tm * BM + row_in_tile;
+            const uint32_t taddr = tmem_base + ((quarter * 32u) << 16) + acc * BN;
+            float *part = a.splits > 1 ? a.ws + ((size_t)tile * a.splits + split) * (BM * BN) + (size_t)row_in_tile * BN
+                                       : nullptr;
+#pragma unroll 1
+            for (int c = 0; c < BN / 32; ++c) {
+                uint32_t r[32];
+                tmem_ld_32x32b_x32(taddr + c * 32, r);
+                tmem_ld_wait();
+                if (part) {
+#pragma unroll
+                    for (int i = 0; i < 8; ++i)
+                        reinterpret_cast<float4 *>(part + c * 32)[i] =
+                            make_float4(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]),
+                                        __uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3]));
+                } else {
+#pragma unroll
+                    for (int g = 0; g < 4; ++g) {
+                        float v[8];
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[8 * g + i]);
+                        epilogue8(a, row, tn * BN + c * 32 + g * 8, v);
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[acc]);
+            acc ^= 1u;
+            if (acc == 0) acc_phase ^= 1u;
+
+            if (a.splits > 1) {
+                // arrival counter: the last split of this tile reduces the partials in split order
+                __threadfence();
+                if (!epi_sync(esync, es_phase, abort, a.err)) break;
+                if (threadIdx.x == 64) {
+                    const uint32_t t = atomicAdd(&a.counters[tile], 1u);
+                    const uint32_t last = (t == a.splits - 1) ? 1u : 0u;
+                    if (last) a.counters[tile] = 0;   // ready for the next launch (stream order)
+                    *last_flag = last;
+                }
+                if (!epi_sync(esync, es_phase, abort, a.err)) break;
+                if (*last_flag) {
+                    __threadfence();
+                    const float *base = a.ws + (size_t)tile * a.splits * (BM * BN) + (size_t)row_in_tile * BN;
+#pragma unroll 1
+                    for (int c = 0; c < BN / 8; ++c) {
+                        float v[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+                        for (uint32_t s = 0; s < a.splits; ++s) {
+                            const float4 *p = reinterpret_cast<const float4 *>(base + (size_t)s * (BM * BN) + c * 8);
+                            const float4 p0 = __ldcg(p), p1 = __ldcg(p + 1);
+                            v[0] += p0.x; v[1] += p0.y; v[2] += p0.z; v[3] += p0.w;
+                            v[4] += p1.x; v[5] += p1.y; v[6] += p1.z; v[7] += p1.w;
+                        }
+                        epilogue8(a, row, tn * BN + c * 8, v);
+                    }
+                }
+                // last_flag is rewritten for the next tile only after every warp has read it
+                if (!epi_sync(esync, es_phase, abort, a.err)) break;
+            }
+        }
+    }
+
+    __syncwarp();
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, C::kTmemCols);
+    }
+}
+
+// ---- CUDA-core fallback: 64 x 64 output tile, 256 threads x (4 x 4), K slabs of 16, any alignment ----------
+__global__ void __launch_bounds__(256) k_gemm_simt(const __half *x, const __half *w, uint32_t ldx, uint32_t ldw,
+                                                   GemmArgs a) {
+    __shared__ float xs[16][64 + 1];
+    __shared__ float ws[16][64 + 1];
+    const uint32_t m0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
+    const uint32_t tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+    float acc[4][4] = {};
+    for (uint32_t k0 = 0; k0 < a.K; k0 += 16) {
+        for (int i = threadIdx.x; i < 16 * 64; i += 256) {
+            const uint32_t kk = i & 15, mm = i >> 4;
+            const uint32_t gm = m0 + mm, gk = k0 + kk;
+            xs[kk][mm] = (gm < a.M && gk < a.K) ? __half2float(x[(size_t)gm * ldx + gk]) : 0.f;
+            const uint32_t nn = i & 63, kw = i >> 6;
+            const uint32_t gn = n0 + nn, gk2 = k0 + kw;
+            ws[kw][nn] = (gn < a.N && gk2 < a.K) ? __half2float(w[(size_t)gk2 * ldw + gn]) : 0.f;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int kk = 0; kk < 16; ++kk) {
+            float xv[4], wv[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                xv[i] = xs[kk][ty * 4 + i];
+                wv[i] = ws[kk][tx * 4 + i];
+            }
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc[i][j] += xv[i] * wv[j];
+        }
+        __syncthreads();
+    }
+    GemmArgs b = a;
+    b.vec = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        float v[8] = {acc[i][0], acc[i][1], acc[i][2], acc[i][3], 0, 0, 0, 0};
+        // columns [n0 + 4 tx, n0 + 4 tx + 4): the scalar epilogue path stops at N; clip to 4 columns here
+        const uint32_t col = n0 + tx * 4;
+        GemmArgs c = b;
+        c.N = min(a.N, col + 4);
+        epilogue8(c, m0 + ty * 4 + i, col, v);
+    }
+}
+
+template <int BN>
+bool set_smem_attr() {
+    static bool done[sh::kMaxDevices] = {};
+    const int d = sh::current_device() % sh::kMaxDevices;
+    if (!done[d]) {
+        if (!sh::cuda_ok(cudaFuncSetAttribute(k_gemm_tc<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              (int)TileCfg<BN>::kSmem),
+                         "cudaFuncSetAttribute(gemm)"))
+            return false;
+        done[d] = true;
+    }
+    return true;
+}
+
+struct Plan {
+    int bn = 0;                   // 0: CUDA-core fallback
+    uint32_t tiles_m = 0, tiles_n = 0, k_blocks = 0, splits = 1, kb_per_split = 0;
+};
+
+Plan make_plan(uint32_t M, uint32_t N, uint32_t K, uint32_t splits_req, int num_sms) {
+    Plan p;
+    p.bn = N > 128 ? 256 : (N > 64 ? 128 : 64);
+    p.tiles_m = (M + BM - 1) / BM;
+    // narrower tiles when the wide ones leave most SMs idle
+    while (p.bn > 64 && (uint64_t)p.tiles_m * ((N + p.bn - 1) / p.bn) * 2 < (uint64_t)num_sms) p.bn >>= 1;
+    p.tiles_n = (N + p.bn - 1) / p.bn;
+    p.k_blocks = (K + BK - 1) / BK;
+    const uint32_t tiles = p.tiles_m * p.tiles_n;
+    uint32_t s = 1;
+    if (splits_req == 0) {
+        if (tiles * 2 <= (uint32_t)num_sms && p.k_blocks >= 8) {
+            s = (uint32_t)num_sms / tiles;
+            s = min(s, p.k_blocks / 4);   // at least 4 K-blocks per split
+            s = min(s, 16u);
+            s = max(s, 1u);
+        }
+    } else {
+        s = min(splits_req, p.k_blocks);
+    }
+    p.kb_per_split = (p.k_blocks + s - 1) / s;
+    p.splits = (p.k_blocks + p.kb_per_split - 1) / p.kb_per_split;
+    return p;
+}
+
+template <int BN>
+int launch_tc(const Plan &p, const CUtensorMap &mx, const CUtensorMap &mw, GemmArgs a, cudaStream_t st) {
+    if (!set_smem_attr<BN>()) return -1;
+    const uint32_t units = p.tiles_m * p.tiles_n * p.splits;
+    const uint32_t grid = min(units, (uint32_t)sh::state().num_sms);
+    k_gemm_tc<BN><<<grid, kThreads, TileCfg<BN>::kSmem, st>>>(mx, mw, a);
+    return sh::cuda_ok(cudaGetLastError(), "sh_gemm launch") ? 0 : -1;
+}
+
+uint32_t smem_of(int bn) {
+    return bn == 256 ? TileCfg<256>::kSmem : bn == 128 ? TileCfg<128>::kSmem : bn == 64 ? TileCfg<64>::kSmem : 0;
+}
+
+}  // namespace
+
+namespace sh {
+
+// Shared by sh_gemm / sh_gemm_mesh / sh_gemm_xmcast_ex / sh_cuda_gemm.
+int gemm_run(uint64_t x, uint64_t w, uint64_t z, uint32_t M, uint32_t N, uint32_t K, uint32_t ldx, uint32_t ldw,
+             uint32_t ldz, uint64_t bias, uint64_t resid, uint32_t ldr, uint32_t flags, uint32_t splits_req,
+             const char *name) {
+    if (M == 0 || N == 0) return 0;
+    if (!x || !w || !z || ldx < K || ldw < N || ldz < N || ((flags & SH_EPI_BIAS) && !bias) ||
+        ((flags & SH_EPI_RESIDUAL) && (!resid || ldr < N))) {
+        set_error(-1, "[%s] bad operands: %ux%ux%u ld %u/%u/%u", name, M, N, K, ldx, ldw, ldz);
+        return -1;
+    }
+    DeviceState &s = state();
+    cudaStream_t st = s.stream;
+    GemmArgs a;
+    memset(&a, 0, sizeof a);
+    a.z = (__half *)z;
+    a.bias = (const __half *)bias;
+    a.resid = (const __half *)resid;
+    a.M = M;
+    a.N = N;
+    a.K = K;
+    a.ldz = ldz;
+    a.ldr = ldr;
+    a.flags = flags & (SH_EPI_ACCUMULATE | SH_EPI_BIAS | SH_EPI_GELU | SH_EPI_RESIDUAL);
+    a.err = s.dev_err;
+    a.vec = aligned16(z) && ldz % 8 == 0 && (!(flags & SH_EPI_BIAS) || aligned16(bias)) &&
+            (!(flags & SH_EPI_RESIDUAL) || (aligned16(resid) && ldr % 8 == 0));
+
+    const bool tc = !(flags & SH_GEMM_SIMT) && K > 0 && aligned16(x) && aligned16(w) && ldx % 8 == 0 &&
+                    ldw % 8 == 0 && encode_tiled() != nullptr;
+    if (!tc) {
+        dim3 grid((N + 63) / 64, (M + 63) / 64);
+        if (grid.y > 65535u) {
+            set_error(-1, "[%s] M = %u too large for the fallback kernel", name, M);
+            return -1;
+        }
+        k_gemm_simt<<<grid, 256, 0, st>>>((const __half *)x, (const __half *)w, ldx, ldw, a);
+        return cuda_ok(cudaGetLastError(), name) ? 0 : -1;
+    }
+    Plan p = make_plan(M, N, K, splits_req, s.num_sms);
+    a.tiles_n = p.tiles_n;
+    a.num_tiles = p.tiles_m * p.tiles_n;
+    a.k_blocks = p.k_blocks;
+    a.splits = p.splits;
+    a.kb_per_split = p.kb_per_split;
+    if (p.splits > 1) {
+        a.ws = workspace((size_t)a.num_tiles * p.splits * BM * p.bn * sizeof(float));
+        a.counters = tile_counters(a.num_tiles);
+        if (!a.ws || !a.counters) return -1;
+    }
+    CUtensorMap mx, mw;
+    if (!make_map_2d(&mx, (const void *)x, M, K, ldx, BM, BK, true) ||
+        !make_map_2d(&mw, (const void *)w, K, N, ldw, BK, 64, true)) {
+        set_error(-1, "[%s] cuTensorMapEncodeTiled failed for %ux%ux%u", name, M, N, K);
+        return -1;
+    }
+    switch (p.bn) {
+        case 256: return launch_tc<256>(p, mx, mw, a, st);
+        case 128: return launch_tc<128>(p, mx, mw, a, st);
+        default: return launch_tc<64>(p, mx, mw, a, st);
+    }
+}
+
+}  // namespace sh
+
+namespace {
+
+void cfg_fill(sh_gemm_cfg *c, const sh_gemm_cfg *in) {   // sh_gemm.inc.c:17-22: NULL / 0 fields -> defaults
+    if (in)
+        *c = *in;
+    else {
+        memset(c, 0, sizeof *c);
+        c->pipeline = 1;
+    }
+    if (!c->tm) c->tm = 256;
+    if (!c->tn) c->tn = 256;
+    if (!c->tk) c->tk = 256;
+}
+
+}  // namespace
+
+extern "C" {
+
+uint32_t sh_gemm_l1_bytes(uint32_t M, uint32_t N, uint32_t K, const sh_gemm_cfg *) {
+    Plan p = make_plan(M, N, K, 0, sh::state().num_sms ? sh::state().num_sms : 148);
+    return smem_of(p.bn);
+}
+
+int sh_gemm(uint64_t x, uint64_t w, uint64_t z, uint32_t M, uint32_t N, uint32_t K, uint32_t ldx, uint32_t ldw,
+            uint32_t ldz, const sh_gemm_cfg *cfg, uint32_t) {
+    sh_gemm_cfg c;
+    cfg_fill(&c, cfg);
+    if (M % c.tm || N % c.tn || K % c.tk) {
+        sh::set_error(-1, "[sh_gemm] shape %ux%ux%u not divisible by tile %ux%ux%u", M, N, K, c.tm, c.tn, c.tk);
+        return -1;
+    }
+    if (c.fmt != SH_FP16) {
+        sh::set_error(-3, "[sh_gemm] fmt %u: only SH_FP16 runs on this backend", c.fmt);
+        return -3;
+    }
+    return sh::gemm_run(x, w, z, M, N, K, ldx, ldw, ldz, 0, 0, 0, c.accumulate ? SH_EPI_ACCUMULATE : 0, 0, "sh_gemm");
+}
+
+int sh_gemm_mesh(uint64_t x, uint64_t w, uint64_t z, uint32_t M, uint32_t N, uint32_t K, uint32_t ldx, uint32_t ldw,
+                 uint32_t ldz, const sh_gemm_cfg *cfg) {
+    sh_gemm_cfg c;
+    cfg_fill(&c, cfg);
+    if (c.tn != c.tm || M % c.tm || N % c.tn || K % c.tk) {
+        sh::set_error(-1, "[sh_gemm_mesh] need tm==tn, M%%tm==0, N%%tn==0, K%%tk==0 (got %ux%ux%u tile %ux%ux%u)", M, N,
+                      K, c.tm, c.tn, c.tk);
+        return -1;
+    }
+    if (c.fmt != SH_FP16) {
+        sh::set_error(-3, "[sh_gemm_mesh] fmt %u: only SH_FP16 runs on this backend", c.fmt);
+        return -3;
+    }
+    return sh::gemm_run(x, w, z, M, N, K, ldx, ldw, ldz, 0, 0, 0, c.accumulate ? SH_EPI_ACCUMULATE : 0, 0,
+                        "sh_gemm_mesh");
+}
+
+uint32_t sh_gemm_xmcast_l1_bytes(uint32_t M, uint32_t N, uint32_t K, const sh_gemm_cfg *cfg, uint32_t) {
+    const uint32_t rows = (cfg && cfg->tm) ? cfg->tm : M;
+    if (rows == 0 || M % rows) return 0xFFFFFFFFu;
+    return sh_gemm_l1_bytes(M, N, K, cfg);
+}
+
+int sh_gemm_xmcast_ex(uint64_t x, uint64_t w, uint64_t z, uint32_t M, uint32_t N, uint32_t K, uint32_t ldx,
+                      uint32_t ldw, uint32_t ldz, const sh_gemm_cfg *cfg, uint32_t mode) {
+    sh_gemm_cfg c;
+    if (cfg)
+        c = *cfg;
+    else
+        memset(&c, 0, sizeof c);
+    const uint32_t rows = c.tm ? c.tm : M;
+    int rc = 0;
+    if (c.fmt & 3)
+        rc = -3;
+    else if (rows == 0 || M % rows || mode > SH_XM_WHOLE)
+        rc = -1;
+    if (rc) {
+        sh::set_error(rc, "[sh_gemm_xmcast] %ux%ux%u tile %u,%u,%u mode %u: no plan (%d)", M, N, K, c.tm, c.tn, c.tk,
+                      mode, rc);
+        return rc;
+    }
+    return sh::gemm_run(x, w, z, M, N, K, ldx, ldw, ldz, 0, 0, 0, c.accumulate ? SH_EPI_ACCUMULATE : 0, 0,
+                        "sh_gemm_xmcast");
+}
+
+int sh_gemm_xmcast(uint64_t x, uint64_t w, uint64_t z, uint32_t M, uint32_t N, uint32_t K, uint32_t ldx, uint32_t ldw,
+                   uint32_t ldz, const sh_gemm_cfg *cfg) {
+    return sh_gemm_xmcast_ex(x, w, z, M, N, K, ldx, ldw, ldz, cfg, SH_XM_AUTO);
+}
+
+int sh_cuda_gemm(uint64_t x, uint64_t w, uint64_t z, uint32_t M, uint32_t N, uint32_t K, uint32_t ldx, uint32_t ldw,
+                 uint32_t ldz, uint64_t bias, uint64_t residual, uint32_t ldr, uint32_t flags, uint32_t splits) {
+    return sh::gemm_run(x, w, z, M, N, K, ldx, ldw, ldz, bias, residual, ldr, flags, splits, "sh_cuda_gemm");
+}
+
+}  // extern "C"

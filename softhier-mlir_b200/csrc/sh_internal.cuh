@@ -1,0 +1,203 @@
+// Internal helpers shared by the translation units of libsh_ops_cuda.so (sm_100a only).
+//
+//  - per-device library state (arena, stream, split-K workspace, device error word, SM count);
+//  - sticky error reporting in the reference's style: a "[sh_xxx] reason" line on stdout and a
+//    negative return code, plus sh_cuda_last_error() for asynchronous CUDA failures;
+//  - inline-PTX wrappers for mbarriers, TMA tensor loads (no cluster broadcast form is ever used),
+//    and the tcgen05 tensor-core / tensor-memory instructions.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stdio.h>
+
+#include "sh_ops.h"
+#include "sh_ops_cuda.h"
+
+namespace sh {
+
+constexpr int kMaxDevices = 16;
+
+struct DeviceState {
+    bool ready = false;
+    int device = -1;
+    int num_sms = 0;
+    size_t smem_optin = 0;
+    // HBM arena: sh_hbm_addr(off) = arena + off
+    char *arena = nullptr;
+    size_t arena_bytes = 0;
+    bool arena_owned = false;
+    size_t malloc_top = 0;               // sh_hbm_malloc carves downwards from the arena's end
+    cudaStream_t stream = nullptr;       // 0 = legacy default stream unless set
+    bool stream_set = false;
+    cudaEvent_t t0 = nullptr, t1 = nullptr;
+    bool timer_running = false;
+    // split-K partial tiles (fp32) and per-tile arrival counters (self-resetting)
+    float *ws = nullptr;
+    size_t ws_bytes = 0;
+    uint32_t *counters = nullptr;
+    size_t counters_len = 0;
+    // device-side error word: kernels store a nonzero code here instead of trapping
+    int *dev_err = nullptr;
+};
+
+DeviceState &state();                 // the calling thread's current device, initialised on first use
+int current_device();
+void set_error(int code, const char *fmt, ...);   // record + print "[sh_...] ..." once per call
+bool cuda_ok(cudaError_t e, const char *where);   // record a CUDA failure, returns e == cudaSuccess
+inline cudaStream_t stream() { return state().stream; }
+float *workspace(size_t bytes);       // grows the split-K workspace (not during stream capture)
+uint32_t *tile_counters(size_t n);
+
+// Device error codes written to DeviceState::dev_err.
+enum DevErr : int { kErrNone = 0, kErrWaitTimeout = 1, kErrBadArgs = 2 };
+
+// ---- driver entry point for tensor maps (no link-time dependency on libcuda) ----------------
+typedef CUresult (*PFN_encodeTiled)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                    const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+PFN_encodeTiled encode_tiled();
+// 2-D fp16 row-major tensor [rows, cols] (leading dim ld elements), box [box_rows, box_cols], 128-B swizzle.
+bool make_map_2d(CUtensorMap *m, const void *base, uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_rows,
+                 uint32_t box_cols, bool swizzle128);
+
+inline bool aligned16(uint64_t p) { return (p & 15u) == 0; }
+
+}  // namespace sh
+
+// ============================================================================================
+// Device-side PTX wrappers
+// ============================================================================================
+#if defined(__CUDACC__)
+
+#ifndef SH_SPIN_CYCLES
+#define SH_SPIN_CYCLES (4000000000ull)   // ~2 s at 2 GHz: every wait gives up after this many SM cycles
+#endif
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait for the phase with the given parity to complete. Gives up after SH_SPIN_CYCLES or when
+// another role of the CTA raised *abort; on a timeout it raises *abort and the device error word.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort, int *dev_err) {
+    const long long t0 = clock64();
+    for (uint32_t it = 0;; ++it) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((it & 63u) == 63u) {
+            if (*abort) return false;
+            if ((unsigned long long)(clock64() - t0) > SH_SPIN_CYCLES) {
+                *abort = 1;
+                if (dev_err) atomicCAS(dev_err, 0, 1);
+                return false;
+            }
+        }
+    }
+}
+
+__device__ __forceinline__ void prefetch_tmap(const CUtensorMap *m) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
+}
+// One 2-D TMA tile load into this CTA's shared memory, completing `bytes` on `bar` (x = innermost coordinate).
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *m, uint64_t *bar, int32_t x, int32_t y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+            smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(m)), "r"(smem_u32(bar)), "r"(x), "r"(y)
+        : "memory");
+}
+
+// ---- tcgen05: tensor memory + UMMA ----------------------------------------------------------
+__device__ __forceinline__ void tmem_alloc(uint32_t *slot, uint32_t ncols) {   // whole warp
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)), "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {   // whole warp
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// D[tmem] (+)= A[smem desc] . B[smem desc], fp16 inputs, fp32 accumulate; issued by one thread.
+__device__ __forceinline__ void umma_f16_ss(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// Arrive (once) on `bar` when every tcgen05.mma this thread issued so far has completed.
+__device__ __forceinline__ void umma_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+// 32 lanes x 32 consecutive fp32 columns: thread t of the warp gets lane (base lane + t).
+__device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+          "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Shared-memory matrix descriptor, 128-byte swizzle (sm_100 descriptor version 1).
+//   K-major operand: rows of 128 B, 8-row groups SBO apart (LBO unused);
+//   MN-major operand: 64-element MN chunks LBO apart, 8-row K groups SBO apart.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+    d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+    d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+    d |= (uint64_t)1 << 46;   // descriptor version for sm_100
+    d |= (uint64_t)2 << 61;   // SWIZZLE_128B
+    return d;
+}
+// Instruction descriptor: fp16 A/B, fp32 D, M x N tile, A and B majorness (0 = K-major, 1 = MN-major).
+__host__ __device__ constexpr uint32_t umma_idesc_f16(uint32_t M, uint32_t N, uint32_t a_mn_major,
+                                                      uint32_t b_mn_major) {
+    return (1u << 4) | (a_mn_major << 15) | (b_mn_major << 16) | ((N >> 3) << 17) | ((M >> 4) << 24);
+}
+
+__device__ __forceinline__ float gelu_tanh(float x) {
+    // 0.5 x (1 + tanh(u)) with u = sqrt(2/pi) (x + 0.044715 x^3), written as x * sigmoid(2u)
+    const float u2 = 1.5957691216057308f * (x + 0.044715f * x * x * x);
+    return x / (1.0f + __expf(-u2));
+}
+
+#endif  // __CUDACC__

@@ -1,0 +1,428 @@
+// Row-wise / elementwise fp16 ops on HBM tensors (reference: runtime/sh_rowops.inc.c:383-465, declared at
+// runtime/sh_ops.h:94-100).
+//
+// The reference stages row blocks through a cluster's TCDM and computes in fp16 SIMD lanes. Here every op is
+// one pass over HBM: row ops (layernorm, softmax) give one warp a whole row held in registers (8 fp16 per
+// 16-byte vector, up to 4096 columns), reduce with warp shuffles in fp32 and store fp16 RNE; elementwise
+// ops stream 16-byte vectors with a grid sized to the SM count. Anything not 16-byte aligned (views with odd
+// element offsets, cols % 8 != 0) takes an element-wise path with the same arithmetic.
+#include "sh_internal.cuh"
+
+namespace {
+
+constexpr int kWarpsPerBlock = 8;
+constexpr int kMaxVecPerLane = 16;   // 16 x 8 x 32 = 4096 columns in registers
+
+struct Vec8 {
+    float v[8];
+};
+
+__device__ __forceinline__ Vec8 load8(const __half *p) {
+    uint4 raw = *reinterpret_cast<const uint4 *>(p);
+    const __half2 *h = reinterpret_cast<const __half2 *>(&raw);
+    Vec8 r;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        float2 f = __half22float2(h[i]);
+        r.v[2 * i] = f.x;
+        r.v[2 * i + 1] = f.y;
+    }
+    return r;
+}
+__device__ __forceinline__ void store8(__half *p, const Vec8 &a) {
+    uint4 raw;
+    __half2 *h = reinterpret_cast<__half2 *>(&raw);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) h[i] = __floats2half2_rn(a.v[2 * i], a.v[2 * i + 1]);
+    *reinterpret_cast<uint4 *>(p) = raw;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// ---- layernorm (optionally fused with the residual add h = a + b) -------------------------------------
+template <int VPL, bool ADD>
+__global__ void __launch_bounds__(kWarpsPerBlock * 32) k_layernorm_vec(__half *y, __half *h, const __half *a,
+                                                                       const __half *b, const __half *g,
+                                                                       const __half *be, uint32_t rows, uint32_t cols,
+                                                                       uint32_t ld, float eps) {
+    const uint32_t lane = threadIdx.x & 31;
+    const uint32_t row = blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5);
+    if (row >= rows) return;
+    const uint32_t cv = cols >> 3;
+    const __half *ar = a + (size_t)row * ld;
+    Vec8 x[VPL];
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+        const uint32_t v = lane + 32 * i;
+        if (v < cv) {
+            x[i] = load8(ar + 8 * v);
+            if (ADD) {
+                Vec8 bb = load8(b + (size_t)row * ld + 8 * v);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) x[i].v[j] = __half2float(__float2half_rn(x[i].v[j] + bb.v[j]));
+                store8(h + (size_t)row * ld + 8 * v, x[i]);
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) s += x[i].v[j];
+        }
+    }
+    const float mean = warp_sum(s) / (float)cols;
+    float q = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+        if (lane + 32 * i < cv) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const float d = x[i].v[j] - mean;
+                q += d * d;
+            }
+        }
+    }
+    const float rstd = rsqrtf(warp_sum(q) / (float)cols + eps);
+    __half *yr = y + (size_t)row * ld;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+        const uint32_t v = lane + 32 * i;
+        if (v < cv) {
+            Vec8 gg = load8(g + 8 * v), bb = load8(be + 8 * v), o;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) o.v[j] = (x[i].v[j] - mean) * rstd * gg.v[j] + bb.v[j];
+            store8(yr + 8 * v, o);
+        }
+    }
+}
+
+// element-wise fallback: one warp per row, three passes over global memory (L1/L2 resident)
+template <bool ADD>
+__global__ void __launch_bounds__(kWarpsPerBlock * 32) k_layernorm_any(__half *y, __half *h, const __half *a,
+                                                                       const __half *b, const __half *g,
+                                                                       const __half *be, uint32_t rows, uint32_t cols,
+                                                                       uint32_t ld, float eps) {
+    const uint32_t lane = threadIdx.x & 31;
+    const uint32_t row = blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5);
+    if (row >= rows) return;
+    const __half *ar = a + (size_t)row * ld;
+    const __half *br = ADD ? b + (size_t)row * ld : nullptr;
+    __half *hr = ADD ? h + (size_t)row * ld : nullptr;
+    auto xin = [&](uint32_t c) -> float {
+        if (ADD) return __half2float(__float2half_rn(__half2float(ar[c]) + __half2float(br[c])));
+        return __half2float(ar[c]);
+    };
+    float s = 0.f;
+    for (uint32_t c = lane; c < cols; c += 32) s += xin(c);
+    const float mean = warp_sum(s) / (float)cols;
+    float q = 0.f;
+    for (uint32_t c = lane; c < cols; c += 32) {
+        const float d = xin(c) - mean;
+        q += d * d;
+    }
+    const float rstd = rsqrtf(warp_sum(q) / (float)cols + eps);
+    __syncwarp();
+    __half *yr = y + (size_t)row * ld;
+    for (uint32_t c = lane; c < cols; c += 32) {
+        const float xv = xin(c);
+        if (ADD) hr[c] = __float2half_rn(xv);
+        yr[c] = __float2half_rn((xv - mean) * rstd * __half2float(g[c]) + __half2float(be[c]));
+    }
+}
+
+// ---- softmax(scale x) per row -----------------------------------------------------------------------------
+template <int VPL>
+__global__ void __launch_bounds__(kWarpsPerBlock * 32) k_softmax_vec(__half *y, const __half *x, uint32_t rows,
+                                                                     uint32_t cols, uint32_t ld, float scale) {
+    const uint32_t lane = threadIdx.x & 31;
+    const uint32_t row = blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5);
+    if (row >= rows) return;
+    const uint32_t cv = cols >> 3;
+    const float s2 = scale * 1.4426950408889634f;   // work in the log2 domain: e^(s x) = 2^(s log2(e) x)
+    Vec8 t[VPL];
+    float m = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+        const uint32_t v = lane + 32 * i;
+        if (v < cv) {
+            t[i] = load8(x + (size_t)row * ld + 8 * v);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                t[i].v[j] *= s2;
+                m = fmaxf(m, t[i].v[j]);
+            }
+        }
+    }
+    m = warp_max(m);
+    float sum = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+        if (lane + 32 * i < cv) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                t[i].v[j] = exp2f(t[i].v[j] - m);
+                sum += t[i].v[j];
+            }
+        }
+    }
+    const float inv = 1.f / warp_sum(sum);
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+        const uint32_t v = lane + 32 * i;
+        if (v < cv) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) t[i].v[j] *= inv;
+            store8(y + (size_t)row * ld + 8 * v, t[i]);
+        }
+    }
+}
+
+__global__ void __launch_bounds__(kWarpsPerBlock * 32) k_softmax_any(__half *y, const __half *x, uint32_t rows,
+                                                                     uint32_t cols, uint32_t ld, float scale) {
+    const uint32_t lane = threadIdx.x & 31;
+    const uint32_t row = blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5);
+    if (row >= rows) return;
+    const float s2 = scale * 1.4426950408889634f;
+    const __half *xr = x + (size_t)row * ld;
+    float m = -INFINITY;
+    for (uint32_t c = lane; c < cols; c += 32) m = fmaxf(m, __half2float(xr[c]) * s2);
+    m = warp_max(m);
+    float sum = 0.f;
+    for (uint32_t c = lane; c < cols; c += 32) sum += exp2f(__half2float(xr[c]) * s2 - m);
+    const float inv = 1.f / warp_sum(sum);
+    __syncwarp();
+    __half *yr = y + (size_t)row * ld;
+    for (uint32_t c = lane; c < cols; c += 32) yr[c] = __float2half_rn(exp2f(__half2float(xr[c]) * s2 - m) * inv);
+}
+
+// ---- elementwise ---------------------------------------------------------------------------------------------
+enum EwOp : int { kGelu = 0, kAdd = 1, kBias = 2, kScale = 3 };
+
+template <int OP>
+__device__ __forceinline__ float ew_apply(float x, float b, float s) {
+    if (OP == kGelu) return gelu_tanh(x);
+    if (OP == kAdd || OP == kBias) return x + b;
+    return x * s;
+}
+
+// rows x cv vectors; `ld` multiple of 8; 64-bit flat index over the vectors
+template <int OP>
+__global__ void k_ew_vec(__half *y, const __half *x, const __half *b, uint32_t rows, uint32_t cv, uint32_t ld,
+                         float s) {
+    const uint64_t total = (uint64_t)rows * cv;
+    for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < total; i += (uint64_t)gridDim.x * blockDim.x) {
+        const uint64_t r = i / cv, c = i - r * cv;
+        const size_t off = r * ld + 8 * c;
+        Vec8 a = load8(x + off), bb;
+        if (OP == kAdd) bb = load8(b + off);
+        if (OP == kBias) bb = load8(b + 8 * c);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) a.v[j] = ew_apply<OP>(a.v[j], (OP == kAdd || OP == kBias) ? bb.v[j] : 0.f, s);
+        store8(y + off, a);
+    }
+}
+
+template <int OP>
+__global__ void k_ew_any(__half *y, const __half *x, const __half *b, uint32_t rows, uint32_t cols, uint32_t ld,
+                         float s) {
+    const uint64_t total = (uint64_t)rows * cols;
+    for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < total; i += (uint64_t)gridDim.x * blockDim.x) {
+        const uint64_t r = i / cols, c = i - r * cols;
+        const size_t off = r * ld + c;
+        float bv = 0.f;
+        if (OP == kAdd) bv = __half2float(b[off]);
+        if (OP == kBias) bv = __half2float(b[c]);
+        y[off] = __float2half_rn(ew_apply<OP>(__half2float(x[off]), bv, s));
+    }
+}
+
+// ---- transpose: 64 x 64 tiles through padded shared memory (bit-exact data movement) ------------------------
+constexpr int TT = 64;
+__global__ void __launch_bounds__(256) k_transpose(__half *dst, const __half *src, uint32_t rows, uint32_t cols,
+                                                   uint32_t ld_src, uint32_t ld_dst, int vec) {
+    __shared__ uint16_t tile[TT][TT + 2];
+    const uint32_t r0 = blockIdx.y * TT, c0 = blockIdx.x * TT;
+    const uint16_t *s16 = reinterpret_cast<const uint16_t *>(src);
+    uint16_t *d16 = reinterpret_cast<uint16_t *>(dst);
+    const bool full = (r0 + TT <= rows) && (c0 + TT <= cols);
+    if (full && vec) {
+        // 64 rows x 8 vectors of 8 elements: 512 vectors, 2 per thread
+        for (int i = threadIdx.x; i < TT * 8; i += 256) {
+            const int r = i >> 3, cv = i & 7;
+            uint4 raw = *reinterpret_cast<const uint4 *>(s16 + (size_t)(r0 + r) * ld_src + c0 + 8 * cv);
+            const uint16_t *e = reinterpret_cast<const uint16_t *>(&raw);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) tile[r][8 * cv + j] = e[j];
+        }
+        __syncthreads();
+        for (int i = threadIdx.x; i < TT * 8; i += 256) {
+            const int c = i >> 3, rv = i & 7;   // output row c (a source column), 8 source rows
+            uint4 raw;
+            uint16_t *e = reinterpret_cast<uint16_t *>(&raw);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) e[j] = tile[8 * rv + j][c];
+            *reinterpret_cast<uint4 *>(d16 + (size_t)(c0 + c) * ld_dst + r0 + 8 * rv) = raw;
+        }
+    } else {
+        for (int i = threadIdx.x; i < TT * TT; i += 256) {
+            const uint32_t r = i / TT, c = i % TT;
+            if (r0 + r < rows && c0 + c < cols) tile[r][c] = s16[(size_t)(r0 + r) * ld_src + c0 + c];
+        }
+        __syncthreads();
+        for (int i = threadIdx.x; i < TT * TT; i += 256) {
+            const uint32_t c = i / TT, r = i % TT;   // consecutive threads: consecutive source rows
+            if (r0 + r < rows && c0 + c < cols) d16[(size_t)(c0 + c) * ld_dst + r0 + r] = tile[r][c];
+        }
+    }
+}
+
+inline bool vec_ok(uint64_t p, uint32_t ld) { return sh::aligned16(p) && (ld % 8 == 0); }
+
+inline uint32_t ew_grid(uint64_t work, int threads) {
+    const uint64_t want = (work + threads - 1) / threads;
+    const uint64_t cap = (uint64_t)sh::state().num_sms * 16;
+    return (uint32_t)(want < cap ? (want ? want : 1) : cap);
+}
+
+template <int OP>
+void launch_ew(uint64_t y, uint64_t x, uint64_t b, uint32_t rows, uint32_t cols, uint32_t ld, float s,
+               const char *name) {
+    if (rows == 0 || cols == 0) return;
+    if (cols > ld) {
+        sh::set_error(-1, "[%s] cols %u > ld %u", name, cols, ld);
+        return;
+    }
+    cudaStream_t st = sh::stream();
+    bool vec = (cols % 8 == 0) && vec_ok(y, ld) && vec_ok(x, ld);
+    if (OP == kAdd) vec = vec && vec_ok(b, ld);
+    if (OP == kBias) vec = vec && sh::aligned16(b);
+    if (vec) {
+        const uint32_t cv = cols / 8;
+        k_ew_vec<OP><<<ew_grid((uint64_t)rows * cv, 256), 256, 0, st>>>((__half *)y, (const __half *)x,
+                                                                        (const __half *)b, rows, cv, ld, s);
+    } else {
+        k_ew_any<OP><<<ew_grid((uint64_t)rows * cols, 256), 256, 0, st>>>((__half *)y, (const __half *)x,
+                                                                          (const __half *)b, rows, cols, ld, s);
+    }
+    sh::cuda_ok(cudaGetLastError(), name);
+}
+
+template <bool ADD, int VPL>
+void ln_vec_launch(uint64_t y, uint64_t h, uint64_t a, uint64_t b, uint64_t g, uint64_t be, uint32_t rows,
+                   uint32_t cols, uint32_t ld, float eps, cudaStream_t st) {
+    const uint32_t grid = (rows + kWarpsPerBlock - 1) / kWarpsPerBlock;
+    k_layernorm_vec<VPL, ADD><<<grid, kWarpsPerBlock * 32, 0, st>>>((__half *)y, (__half *)h, (const __half *)a,
+                                                                     (const __half *)b, (const __half *)g,
+                                                                     (const __half *)be, rows, cols, ld, eps);
+}
+
+template <bool ADD>
+void launch_layernorm(uint64_t y, uint64_t h, uint64_t a, uint64_t b, uint64_t g, uint64_t be, uint32_t rows,
+                      uint32_t cols, uint32_t ld, float eps, const char *name) {
+    if (rows == 0 || cols == 0) return;
+    if (cols > ld) {
+        sh::set_error(-1, "[%s] cols %u > ld %u", name, cols, ld);
+        return;
+    }
+    cudaStream_t st = sh::stream();
+    bool vec = cols % 8 == 0 && cols <= 32u * 8u * kMaxVecPerLane && vec_ok(y, ld) && vec_ok(a, ld) &&
+               sh::aligned16(g) && sh::aligned16(be);
+    if (ADD) vec = vec && vec_ok(h, ld) && vec_ok(b, ld);
+    if (vec) {
+        const int vpl = (int)((cols / 8 + 31) / 32);
+        switch (vpl) {
+#define SH_LN_CASE(n) \
+    case n: ln_vec_launch<ADD, n>(y, h, a, b, g, be, rows, cols, ld, eps, st); break;
+            SH_LN_CASE(1) SH_LN_CASE(2) SH_LN_CASE(3) SH_LN_CASE(4) SH_LN_CASE(5) SH_LN_CASE(6) SH_LN_CASE(7)
+            SH_LN_CASE(8) SH_LN_CASE(9) SH_LN_CASE(10) SH_LN_CASE(11) SH_LN_CASE(12) SH_LN_CASE(13) SH_LN_CASE(14)
+            SH_LN_CASE(15) SH_LN_CASE(16)
+#undef SH_LN_CASE
+            default: break;
+        }
+    } else {
+        const uint32_t grid = (rows + kWarpsPerBlock - 1) / kWarpsPerBlock;
+        k_layernorm_any<ADD><<<grid, kWarpsPerBlock * 32, 0, st>>>((__half *)y, (__half *)h, (const __half *)a,
+                                                                   (const __half *)b, (const __half *)g,
+                                                                   (const __half *)be, rows, cols, ld, eps);
+    }
+    sh::cuda_ok(cudaGetLastError(), name);
+}
+
+template <int VPL>
+void sm_vec_launch(uint64_t y, uint64_t x, uint32_t rows, uint32_t cols, uint32_t ld, float scale, cudaStream_t st) {
+    const uint32_t grid = (rows + kWarpsPerBlock - 1) / kWarpsPerBlock;
+    k_softmax_vec<VPL><<<grid, kWarpsPerBlock * 32, 0, st>>>((__half *)y, (const __half *)x, rows, cols, ld, scale);
+}
+
+}  // namespace
+
+extern "C" {
+
+void sh_layernorm(uint64_t y, uint64_t x, uint64_t gamma, uint64_t beta, uint32_t rows, uint32_t cols, uint32_t ld,
+                  float eps, uint32_t) {
+    launch_layernorm<false>(y, 0, x, 0, gamma, beta, rows, cols, ld, eps, "sh_layernorm");
+}
+
+void sh_cuda_add_layernorm(uint64_t h, uint64_t y, uint64_t a, uint64_t b, uint64_t gamma, uint64_t beta,
+                           uint32_t rows, uint32_t cols, uint32_t ld, float eps) {
+    launch_layernorm<true>(y, h, a, b, gamma, beta, rows, cols, ld, eps, "sh_cuda_add_layernorm");
+}
+
+void sh_softmax_rows(uint64_t y, uint64_t x, uint32_t rows, uint32_t cols, uint32_t ld, float scale, uint32_t) {
+    if (rows == 0 || cols == 0) return;
+    if (cols > ld) {
+        sh::set_error(-1, "[sh_softmax_rows] cols %u > ld %u", cols, ld);
+        return;
+    }
+    cudaStream_t st = sh::stream();
+    const bool vec = cols % 8 == 0 && cols <= 32u * 8u * kMaxVecPerLane && vec_ok(y, ld) && vec_ok(x, ld);
+    if (vec) {
+        switch ((int)((cols / 8 + 31) / 32)) {
+#define SH_SM_CASE(n) \
+    case n: sm_vec_launch<n>(y, x, rows, cols, ld, scale, st); break;
+            SH_SM_CASE(1) SH_SM_CASE(2) SH_SM_CASE(3) SH_SM_CASE(4) SH_SM_CASE(5) SH_SM_CASE(6) SH_SM_CASE(7)
+            SH_SM_CASE(8) SH_SM_CASE(9) SH_SM_CASE(10) SH_SM_CASE(11) SH_SM_CASE(12) SH_SM_CASE(13) SH_SM_CASE(14)
+            SH_SM_CASE(15) SH_SM_CASE(16)
+#undef SH_SM_CASE
+            default: break;
+        }
+    } else {
+        const uint32_t grid = (rows + kWarpsPerBlock - 1) / kWarpsPerBlock;
+        k_softmax_any<<<grid, kWarpsPerBlock * 32, 0, st>>>((__half *)y, (const __half *)x, rows, cols, ld, scale);
+    }
+    sh::cuda_ok(cudaGetLastError(), "sh_softmax_rows");
+}
+
+void sh_gelu(uint64_t y, uint64_t x, uint32_t rows, uint32_t cols, uint32_t ld, uint32_t) {
+    launch_ew<kGelu>(y, x, 0, rows, cols, ld, 0.f, "sh_gelu");
+}
+void sh_add(uint64_t y, uint64_t a, uint64_t b, uint32_t rows, uint32_t cols, uint32_t ld, uint32_t) {
+    launch_ew<kAdd>(y, a, b, rows, cols, ld, 0.f, "sh_add");
+}
+void sh_add_bias(uint64_t y, uint64_t x, uint64_t bias_row, uint32_t rows, uint32_t cols, uint32_t ld, uint32_t) {
+    launch_ew<kBias>(y, x, bias_row, rows, cols, ld, 0.f, "sh_add_bias");
+}
+void sh_scale(uint64_t y, uint64_t x, uint32_t rows, uint32_t cols, uint32_t ld, float s, uint32_t) {
+    launch_ew<kScale>(y, x, 0, rows, cols, ld, s, "sh_scale");
+}
+
+void sh_transpose(uint64_t dst, uint64_t src, uint32_t rows, uint32_t cols, uint32_t ld_src, uint32_t ld_dst,
+                  uint32_t) {
+    if (rows == 0 || cols == 0) return;
+    if (cols > ld_src || rows > ld_dst) {
+        sh::set_error(-1, "[sh_transpose] %ux%u with ld_src %u ld_dst %u", rows, cols, ld_src, ld_dst);
+        return;
+    }
+    const int vec = vec_ok(src, ld_src) && vec_ok(dst, ld_dst);
+    dim3 grid((cols + TT - 1) / TT, (rows + TT - 1) / TT);
+    k_transpose<<<grid, 256, 0, sh::stream()>>>((__half *)dst, (const __half *)src, rows, cols, ld_src, ld_dst, vec);
+    sh::cuda_ok(cudaGetLastError(), "sh_transpose");
+}
+
+}  // extern "C"

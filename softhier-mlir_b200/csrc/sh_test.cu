@@ -1,0 +1,185 @@
+// Test helpers of the operator library (reference: runtime/sh_test.inc.c:2-115, sh_rt.inc.c:31-59; declared at
+// runtime/sh_ops.h:220-240).
+//
+// The fills run on the GPU: each thread jumps the 32-bit LCG to the start of its chunk with the composed affine
+// map (log2 steps) and then steps sequentially, so the bytes equal the reference's single-core loop exactly.
+// Dumps and checks read the device tensor back and print the reference's line formats.
+#include <math.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <vector>
+
+#include "sh_internal.cuh"
+
+namespace {
+
+constexpr uint32_t kA = 1664525u, kC = 1013904223u, kSeedXor = 0x9e3779b9u;
+
+struct Affine {
+    uint32_t a, c;
+};
+__host__ __device__ inline Affine compose(Affine first, Affine then) {
+    return Affine{then.a * first.a, then.a * first.c + then.c};
+}
+// the map that advances the state by n steps
+__host__ __device__ inline Affine lcg_jump(uint64_t n) {
+    Affine acc{1u, 0u}, p{kA, kC};
+    while (n) {
+        if (n & 1) acc = compose(acc, p);
+        p = compose(p, p);
+        n >>= 1;
+    }
+    return acc;
+}
+
+constexpr uint32_t kChunk = 64;   // elements per thread
+
+__global__ void k_fill_lcg(__half *a, uint32_t rows, uint32_t cols, uint32_t ld, uint32_t seed, int lo, uint32_t span,
+                           float scale) {
+    const uint64_t total = (uint64_t)rows * cols;
+    const uint64_t start = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) * kChunk;
+    if (start >= total) return;
+    const Affine j = lcg_jump(start);
+    uint32_t s = j.a * (seed ^ kSeedXor) + j.c;   // state before element `start` is drawn
+    uint64_t r = start / cols, c = start - r * cols;
+    const uint64_t end = start + kChunk < total ? start + kChunk : total;
+    for (uint64_t i = start; i < end; ++i) {
+        s = s * kA + kC;
+        const int v = lo + (int)((s >> 8) % span);
+        a[r * ld + c] = __float2half_rn((float)v * scale);
+        if (++c == cols) {
+            c = 0;
+            ++r;
+        }
+    }
+}
+
+__global__ void k_fill_parity(uint16_t *a, uint32_t rows, uint32_t cols, uint32_t ld, uint16_t even, uint16_t odd) {
+    const uint64_t total = (uint64_t)rows * cols;
+    for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < total; i += (uint64_t)gridDim.x * blockDim.x) {
+        const uint64_t r = i / cols, c = i - r * cols;
+        a[r * ld + c] = (c & 1) ? odd : even;
+    }
+}
+
+uint32_t host_lcg(uint32_t *s) {
+    *s = *s * kA + kC;
+    return *s >> 8;
+}
+
+bool read_elem(uint64_t a, uint64_t idx, uint16_t *out) {
+    return sh::cuda_ok(cudaMemcpy(out, (const void *)(a + idx * 2), 2, cudaMemcpyDeviceToHost), "sh_test read");
+}
+
+}  // namespace
+
+extern "C" {
+
+float sh_fp16_to_f32(uint16_t h) {
+    __half_raw r;
+    r.x = h;
+    return __half2float(__half(r));
+}
+
+uint16_t sh_f32_to_fp16(float f) {   // round to nearest even, like the reference's software conversion
+    __half_raw r = __half_raw(__float2half_rn(f));
+    return r.x;
+}
+
+void sh_test_fill_fp16(uint64_t a, uint32_t rows, uint32_t cols, uint32_t ld, uint32_t seed, int lo, int hi,
+                       float scale) {
+    if (rows == 0 || cols == 0) return;
+    const uint64_t total = (uint64_t)rows * cols;
+    const uint64_t threads = (total + kChunk - 1) / kChunk;
+    const uint32_t grid = (uint32_t)((threads + 255) / 256);
+    k_fill_lcg<<<grid, 256, 0, sh::stream()>>>((__half *)a, rows, cols, ld, seed, lo, (uint32_t)(hi - lo + 1), scale);
+    sh::cuda_ok(cudaGetLastError(), "sh_test_fill_fp16");
+}
+
+void sh_test_fill_int_fp16(uint64_t a, uint32_t rows, uint32_t cols, uint32_t ld, uint32_t seed, int lo, int hi) {
+    sh_test_fill_fp16(a, rows, cols, ld, seed, lo, hi, 1.0f);
+}
+
+void sh_test_fill_colparity_fp16(uint64_t a, uint32_t rows, uint32_t cols, uint32_t ld, uint32_t even, uint32_t odd) {
+    if (rows == 0 || cols == 0) return;
+    k_fill_parity<<<1024, 256, 0, sh::stream()>>>((uint16_t *)a, rows, cols, ld, (uint16_t)even, (uint16_t)odd);
+    sh::cuda_ok(cudaGetLastError(), "sh_test_fill_colparity_fp16");
+}
+
+void sh_test_fill_const_fp16(uint64_t a, uint32_t rows, uint32_t cols, uint32_t ld, uint32_t bits) {
+    sh_test_fill_colparity_fp16(a, rows, cols, ld, bits, bits);
+}
+
+void sh_test_dump_samples(uint64_t a, uint32_t rows, uint32_t cols, uint32_t ld, uint32_t seed, uint32_t nsamples,
+                          const char *tag) {
+    if (!sh::cuda_ok(cudaStreamSynchronize(sh::stream()), "sh_test_dump_samples")) return;
+    uint32_t s = seed ^ kSeedXor;
+    for (uint32_t n = 0; n < nsamples; ++n) {
+        const uint32_t i = host_lcg(&s) % rows, j = host_lcg(&s) % cols;
+        uint16_t v = 0;
+        if (!read_elem(a, (uint64_t)i * ld + j, &v)) return;
+        printf("%s %u %u %04x\n", tag, i, j, (uint32_t)v);
+    }
+    fflush(stdout);
+}
+
+void sh_test_dump_samples_idx(uint64_t a, uint32_t rows, uint32_t cols, uint32_t ld, uint32_t seed, uint32_t nsamples,
+                              const char *tag, uint32_t idx) {
+    char t[64];
+    snprintf(t, sizeof t, "%s%u", tag, idx);
+    sh_test_dump_samples(a, rows, cols, ld, seed, nsamples, t);
+}
+
+uint32_t sh_test_check_gemm(uint64_t x, uint64_t w, uint64_t z, uint32_t M, uint32_t N, uint32_t K, uint32_t ldx,
+                            uint32_t ldw, uint32_t ldz, uint32_t nsamples, float tol, float z0, const char *tag) {
+    if (!sh::cuda_ok(cudaStreamSynchronize(sh::stream()), "sh_test_check_gemm")) return nsamples;
+    uint32_t s = 0xC0FFEEu, bad = 0;
+    float maxdiff = 0.f;
+    std::vector<uint16_t> xr(K), wc(K);
+    for (uint32_t n = 0; n < nsamples; ++n) {
+        const uint32_t i = (n * 7919u + host_lcg(&s)) % M, j = (n * 104729u + host_lcg(&s)) % N;
+        if (!sh::cuda_ok(cudaMemcpy(xr.data(), (const void *)(x + (uint64_t)i * ldx * 2), K * 2, cudaMemcpyDeviceToHost),
+                         "sh_test_check_gemm") ||
+            !sh::cuda_ok(cudaMemcpy2D(wc.data(), 2, (const void *)(w + (uint64_t)j * 2), (size_t)ldw * 2, 2, K,
+                                      cudaMemcpyDeviceToHost),
+                         "sh_test_check_gemm"))
+            return nsamples;
+        float acc = z0;
+        for (uint32_t k = 0; k < K; ++k) acc += sh_fp16_to_f32(xr[k]) * sh_fp16_to_f32(wc[k]);
+        uint16_t zv = 0;
+        if (!read_elem(z, (uint64_t)i * ldz + j, &zv)) return nsamples;
+        const float got = sh_fp16_to_f32(zv);
+        const float d = fabsf(got - acc);
+        if (d > maxdiff) maxdiff = d;
+        if (d > tol) {
+            if (bad < 4) printf("  mismatch z[%u,%u] got %f want %f\n", i, j, got, acc);
+            ++bad;
+        }
+    }
+    printf("%s samples=%u bad=%u maxdiff=%f %s\n", tag, nsamples, bad, maxdiff, bad ? "FAIL" : "PASS");
+    fflush(stdout);
+    return bad;
+}
+
+uint32_t sh_test_check_const_fp16(uint64_t a, uint32_t rows, uint32_t cols, uint32_t ld, uint32_t bits, uint32_t tol,
+                                  const char *tag) {
+    if (!sh::cuda_ok(cudaStreamSynchronize(sh::stream()), "sh_test_check_const_fp16")) return 0;
+    std::vector<uint16_t> h((size_t)rows * cols);
+    if (rows && cols &&
+        !sh::cuda_ok(cudaMemcpy2D(h.data(), (size_t)cols * 2, (const void *)a, (size_t)ld * 2, (size_t)cols * 2, rows,
+                                  cudaMemcpyDeviceToHost),
+                     "sh_test_check_const_fp16"))
+        return 0;
+    uint32_t ok = 0;
+    for (size_t i = 0; i < h.size(); ++i) {
+        int d = (int)h[i] - (int)bits;
+        if (d < 0) d = -d;
+        if ((uint32_t)d <= tol) ++ok;
+    }
+    printf("%s_CHECK ok=%u/%u %s_%s\n", tag, ok, rows * cols, tag, ok == rows * cols ? "PASS" : "FAIL");
+    fflush(stdout);
+    return ok;
+}
+
+}  // extern "C"

@@ -1,0 +1,126 @@
+"""Batched SigLIP / ViT pre-LN encoder on the library's C ABI (the workload of frontend/siglip.py:133-168, run over
+a batch of B sequences of S tokens at once).
+
+Per layer, 7 launches on device-resident activations [B*S, D] (row-major fp16):
+    ln1 = LN(x)                                   sh_layernorm
+    qkv = ln1 . [wq|wk|wv] + [bq|bk|bv]           sh_cuda_gemm, bias epilogue (one N = 3D GEMM; q/k/v are the
+                                                  column slices the attention reads with ld = 3D, the packed
+                                                  layout of tests/filecheck/attention_translate.mlir)
+    o   = attention(q, k, v) per sequence, head   sh_cuda_attention_batched
+    h   = x + o . wo + bo                         sh_cuda_gemm, bias + residual epilogue
+    ln2 = LN(h)                                   sh_layernorm
+    g   = gelu(ln2 . w1 + b1)                     sh_cuda_gemm, bias + GELU epilogue
+    out = h + g . w2 + b2                         sh_cuda_gemm, bias + residual epilogue
+This is the reference layer (siglip_ref.py:20-45) with the frontend's add_bias / gelu / add ops folded into the
+GEMM epilogues, so each intermediate is rounded to fp16 once instead of after every op.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import numpy as np
+
+from . import lib as L
+from .runtime import Runtime
+
+
+@dataclass
+class LayerWeights:
+    wqkv: int
+    bqkv: int
+    wo: int
+    bo: int
+    w1: int
+    b1: int
+    w2: int
+    b2: int
+    g1: int
+    be1: int
+    g2: int
+    be2: int
+
+
+@dataclass
+class Activations:
+    B: int
+    S: int
+    D: int
+    F: int
+    x: int
+    ln1: int
+    qkv: int
+    o: int
+    h: int
+    ln2: int
+    g: int
+    out: int
+    extra: dict = field(default_factory=dict)
+
+
+def upload_layer(rt: Runtime, p: dict) -> LayerWeights:
+    """Parameters in the reference's layout (weights [in, out], 1 x cols rows) -> device; q/k/v weights and biases
+    are concatenated along the output columns."""
+    f16 = lambda a: np.asarray(a, dtype=np.float16)  # noqa: E731
+    wqkv = np.concatenate([f16(p["wq"]), f16(p["wk"]), f16(p["wv"])], axis=1)
+    bqkv = np.concatenate([f16(p["bq"]), f16(p["bk"]), f16(p["bv"])], axis=1)
+    up = rt.upload
+    return LayerWeights(wqkv=up(wqkv), bqkv=up(bqkv), wo=up(p["wo"]), bo=up(p["bo"]), w1=up(p["w1"]), b1=up(p["b1"]),
+                        w2=up(p["w2"]), b2=up(p["b2"]), g1=up(p["g1"]), be1=up(p["be1"]), g2=up(p["g2"]),
+                        be2=up(p["be2"]))
+
+
+def alloc_activations(rt: Runtime, B: int, S: int, D: int, F: int) -> Activations:
+    M = B * S
+    a = rt.alloc
+    return Activations(B=B, S=S, D=D, F=F, x=a(M, D), ln1=a(M, D), qkv=a(M, 3 * D), o=a(M, D), h=a(M, D),
+                       ln2=a(M, D), g=a(M, F), out=a(M, D))
+
+
+def layer_forward(lib, act: Activations, w: LayerWeights, heads: int, eps: float, scale: float,
+                  x: int | None = None, out: int | None = None) -> int:
+    """Enqueue one layer on the library stream: reads x (default act.x), writes out (default act.out).
+    Returns 0 or the first negative return code."""
+    B, S, D, F = act.B, act.S, act.D, act.F
+    M = B * S
+    x = act.x if x is None else x
+    out = act.out if out is None else out
+    A = L.SH_ALL
+    lib.sh_layernorm(act.ln1, x, w.g1, w.be1, M, D, D, eps, A)
+    rc = lib.sh_cuda_gemm(act.ln1, w.wqkv, act.qkv, M, 3 * D, D, D, 3 * D, 3 * D, w.bqkv, 0, 0, L.EPI_BIAS, 0)
+    rc = rc or lib.sh_cuda_attention_batched(act.qkv, act.qkv + 2 * D, act.qkv + 4 * D, act.o, S, D, heads,
+                                             3 * D, 3 * D, 3 * D, D, scale, B)
+    rc = rc or lib.sh_cuda_gemm(act.o, w.wo, act.h, M, D, D, D, D, D, w.bo, x, D, L.EPI_BIAS | L.EPI_RESIDUAL, 0)
+    lib.sh_layernorm(act.ln2, act.h, w.g2, w.be2, M, D, D, eps, A)
+    rc = rc or lib.sh_cuda_gemm(act.ln2, w.w1, act.g, M, F, D, D, F, F, w.b1, 0, 0, L.EPI_BIAS | L.EPI_GELU, 0)
+    rc = rc or lib.sh_cuda_gemm(act.g, w.w2, out, M, D, F, F, D, D, w.b2, act.h, D, L.EPI_BIAS | L.EPI_RESIDUAL, 0)
+    return rc
+
+
+def encoder_forward(lib, act: Activations, layers: list[LayerWeights], heads: int, eps: float, scale: float) -> int:
+    """All layers; the residual stream ping-pongs between act.x and act.out. Returns the address of the result."""
+    cur, nxt = act.x, act.out
+    for w in layers:
+        rc = layer_forward(lib, act, w, heads, eps, scale, x=cur, out=nxt)
+        if rc:
+            raise RuntimeError(f"encoder layer failed with {rc}")
+        cur, nxt = nxt, cur
+    return cur
+
+
+def launches_per_layer() -> int:
+    return 7
+
+
+def run_layer_once(rt: Runtime, x: np.ndarray, p: dict, heads: int, eps: float = 1e-6,
+                   scale: float = 0.125) -> np.ndarray:
+    """One layer on one sequence (host arrays in, host array out)."""
+    S, D = x.shape
+    F = np.asarray(p["w1"]).shape[1]
+    rt.reset()
+    w = upload_layer(rt, p)
+    act = alloc_activations(rt, 1, S, D, F)
+    rt.put(act.x, x)
+    rc = layer_forward(rt.lib, act, w, heads, eps, scale)
+    if rc:
+        raise RuntimeError(f"layer_forward returned {rc}")
+    return rt.get(act.out, S, D)

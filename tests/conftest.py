@@ -30,5 +30,5 @@ def gpu_lib():
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
     from softhier_cuda import runtime
-    rt = runtime.Runtime.get(arena_bytes=2 << 30)
+    rt = runtime.Runtime.open(arena_bytes=2 << 30)
     return rt
