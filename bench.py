@@ -1,0 +1,416 @@
+#!/usr/bin/env python3
+"""Headline benchmark: SigLIP-base encoder images/s on B200 through libsh_ops_cuda.so.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload encoder|gemm512|rowops]
+
+Workload: 12 pre-LN SigLIP-base layers (S=256, D=768, 12 heads x 64, FFN 3072, tanh-GELU,
+scale 1/8, eps 1e-6), a global batch of 512 sequences sharded data-parallel over the N ranks (B = 512 / N per GPU,
+weights replicated: every rank generates the same per-layer N(0, 0.02) weights from the same LCG seeds; x ~ N(0,1)).
+One step = one forward pass over the rank's shard, 84 library launches replayed from a CUDA graph. The activations
+(201 MB per tensor at B=512) are larger than the 126 MB L2, so no flush is needed between steps.
+
+One JSON line on rank 0 (the contract of this repository's driver): `value` is the whole-job images/s with the
+inputs resident in HBM, timed with CUDA events over K steps between barriers, max over ranks; `e2e` is the same
+metric through the public API with the input batch copied from pinned host memory and the result copied back
+inside every timed step; `roofline` describes the dominant kernel (the tcgen05 GEMM), `kernels` the per-kernel
+breakdown measured with CUDA events around each launch; `cpu_baseline` times the numpy oracle of the same layer on
+the host cores (rank 0, N=1 only). `--impl reference` times that CPU implementation alone (there is no GPU
+implementation in the reference: it targets a simulated RISC-V accelerator).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+PKG = ROOT / "softhier-mlir_b200"
+for _p in (str(ROOT), str(PKG)):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+S, D, F, H, NLAYERS = 256, 768, 3072, 12, 12
+GLOBAL_BATCH = 512
+EPS, SCALE = 1e-6, 0.125
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+# ---- environment -------------------------------------------------------------------------------------------------
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def init_dist(world: int, local: int):
+    import torch
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=torch.device("cuda", local))
+
+
+def barrier(world: int):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(v: float, world: int) -> float:
+    if world == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def peaks() -> tuple[dict, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text()), "measured"
+        except ValueError:
+            pass
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def profile_traffic(kernel: str) -> float | None:
+    """DRAM bytes per launch of `kernel` at the bench shape, from the committed ncu summary in profiles/
+    (a line `traffic_bytes_per_launch <kernel> <bytes>`), or None."""
+    for f in sorted((ROOT / "profiles").glob("*.md")):
+        for m in re.finditer(r"traffic_bytes_per_launch\s+(\S+)\s+([0-9.eE+]+)", f.read_text()):
+            if m.group(1) == kernel:
+                return float(m.group(2))
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 100 ms while the timed region runs."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, local: int):
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+        self.index = vis.split(",")[local] if vis else str(local)
+        self.proc = None
+        self.lines: list[str] = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-i", self.index, "-lms", "100"], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.thread.join(timeout=2)
+        sm, mx, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 7:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx = float(parts[1])
+            except ValueError:
+                continue
+            for nm, val in zip(names, parts[3:7]):
+                if val.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "samples": len(sm),
+                "reasons": sorted(reasons)}
+
+
+# ---- the GPU arm -----------------------------------------------------------------------------------------------------
+def setup_encoder(rt, B: int, rank: int):
+    """Device weights (identical on every rank) and activations for a shard of B sequences."""
+    from softhier_cuda import encoder
+    lib = rt.lib
+    layers = []
+    for li in range(NLAYERS):
+        a = rt.alloc
+        w = encoder.LayerWeights(wqkv=a(D, 3 * D), bqkv=a(1, 3 * D), wo=a(D, D), bo=a(1, D), w1=a(D, F), b1=a(1, F),
+                                 w2=a(F, D), b2=a(1, D), g1=a(1, D), be1=a(1, D), g2=a(1, D), be2=a(1, D))
+        seed = 7000 + 16 * li
+        lib.sh_cuda_fill_normal_fp16(w.wqkv, D, 3 * D, 3 * D, seed + 0, 0.0, 0.02)
+        lib.sh_cuda_fill_normal_fp16(w.wo, D, D, D, seed + 1, 0.0, 0.02)
+        lib.sh_cuda_fill_normal_fp16(w.w1, D, F, F, seed + 2, 0.0, 0.02)
+        lib.sh_cuda_fill_normal_fp16(w.w2, F, D, D, seed + 3, 0.0, 0.02)
+        for b, n in ((w.bqkv, 3 * D), (w.bo, D), (w.b1, F), (w.b2, D), (w.be1, D), (w.be2, D)):
+            lib.sh_test_fill_const_fp16(b, 1, n, n, 0x0000)
+        for g in (w.g1, w.g2):
+            lib.sh_test_fill_const_fp16(g, 1, D, D, 0x3C00)
+        layers.append(w)
+    act = encoder.alloc_activations(rt, B, S, D, F)
+    x_in = rt.alloc(B * S, D)
+    lib.sh_cuda_fill_normal_fp16(x_in, B * S, D, D, 100 + rank, 0.0, 1.0)
+    return layers, act, x_in
+
+
+def run_ours(args, rank: int, world: int, local: int) -> dict | None:
+    import torch
+    from softhier_cuda import encoder
+    from softhier_cuda.runtime import Runtime
+
+    init_dist(world, local)
+    if GLOBAL_BATCH % world:
+        raise SystemExit(f"global batch {GLOBAL_BATCH} does not split over {world} ranks")
+    B = GLOBAL_BATCH // world
+    M = B * S
+    arena = (13 * M * D + (M * F - M * D) + NLAYERS * (4 * D * D + 2 * D * F + 10 * F)) * 2 + (256 << 20)
+    rt = Runtime.open(local, arena_bytes=arena)
+    lib = rt.lib
+    layers, act, x_in = setup_encoder(rt, B, rank)
+    rt.check()
+    sched, res = encoder.encoder_schedule(lib, act, layers, H, EPS, SCALE, x_in)
+    stream = torch.cuda.Stream(device=local)
+    rt.activate(stream)
+
+    def enqueue():
+        for kind, fn in sched:
+            rc = fn()
+            if rc:
+                raise RuntimeError(f"{kind} returned {rc}")
+
+    with torch.cuda.stream(stream):
+        for _ in range(max(1, args.warmup)):
+            enqueue()
+    stream.synchronize()
+    rt.check()
+
+    # ---- per-kernel breakdown: CUDA events around every launch of 2 eager steps --------------------------------
+    if args.debug:
+        log("library stream", lib.sh_cuda_get_stream(), "bench stream", stream.cuda_stream)
+    kinds = [k for k, _ in sched]
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(len(sched) + 1)]
+    per_kind: dict[str, list[float]] = {}
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            evs[0].record(stream)
+            for i, (_, fn) in enumerate(sched):
+                fn()
+                evs[i + 1].record(stream)
+            stream.synchronize()
+            for i, k in enumerate(kinds):
+                per_kind.setdefault(k, []).append(evs[i].elapsed_time(evs[i + 1]))
+    rt.check()
+    if args.debug:
+        log("breakdown ms per kind:", {k: round(sum(v), 3) for k, v in per_kind.items()})
+
+    # ---- CUDA graph of one step ------------------------------------------------------------------------------------
+    graph = None
+    if not args.no_graph:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            lib.sh_cuda_set_stream(torch.cuda.current_stream().cuda_stream)
+            enqueue()
+        lib.sh_cuda_set_stream(stream.cuda_stream)
+
+    def step():
+        with torch.cuda.stream(stream):   # graph replays and eager launches both go to `stream`
+            if graph is not None:
+                graph.replay()
+            else:
+                enqueue()
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    stream.synchronize()
+    rt.check()
+
+    # ---- timed region: inputs resident in HBM --------------------------------------------------------------------------
+    clocks = ClockSampler(local)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    clocks.start()
+    time.sleep(0.05)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    e1.synchronize()
+    clock_info = clocks.stop()
+    barrier(world)
+    ms = max_over_ranks(e0.elapsed_time(e1), world)
+    rt.check()
+    value = GLOBAL_BATCH * args.steps / (ms / 1e3)
+
+    # ---- e2e: host input -> device -> encoder -> host output every step ----------------------------------------------
+    host_in = torch.empty((M, D), dtype=torch.float16, pin_memory=True)
+    host_out = torch.empty((M, D), dtype=torch.float16, pin_memory=True)
+    host_in.copy_(rt.view(x_in, M, D).cpu())
+    dev_in, dev_out = rt.view(x_in, M, D), rt.view(res, M, D)
+    e2e_steps = max(3, args.steps // 2)
+    barrier(world)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        with torch.cuda.stream(stream):
+            dev_in.copy_(host_in, non_blocking=True)
+        step()
+        with torch.cuda.stream(stream):
+            host_out.copy_(dev_out, non_blocking=True)
+    e1.record(stream)
+    e1.synchronize()
+    barrier(world)
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1), world)
+    e2e_value = GLOBAL_BATCH * e2e_steps / (e2e_ms / 1e3)
+    rt.check()
+
+    # ---- roofline of the dominant kernel and the per-kernel table -------------------------------------------------------
+    pk, src = peaks()
+    kernels = {}
+    for k, times in per_kind.items():
+        n_per_step = kinds.count(k)
+        t_launch = sum(times) / len(times) * 1e-3   # s per launch (one entry per launch)
+        flops, nbytes = encoder.op_work(k, B, S, D, F, H)
+        kernels[k] = {"launches_per_step": n_per_step, "ms_per_launch": round(t_launch * 1e3, 4),
+                      "tflops": round(flops / t_launch / 1e12, 1), "gbs": round(nbytes / t_launch / 1e9, 1)}
+    gemm_kinds = [k for k in kernels if k.startswith("gemm")]
+    gemm_flops = sum(encoder.op_work(k, B, S, D, F, H)[0] * kernels[k]["launches_per_step"] for k in gemm_kinds)
+    gemm_time = sum(kernels[k]["ms_per_launch"] * 1e-3 * kernels[k]["launches_per_step"] for k in gemm_kinds)
+    gemm_launches = sum(kernels[k]["launches_per_step"] for k in gemm_kinds)
+    achieved = gemm_flops / gemm_time / 1e12
+    peak = pk.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"])
+    traffic = profile_traffic("gemm_fc1")
+    roofline = {"kernel": "k_gemm_tc (tcgen05 GEMM, 4 per layer)", "bound": "tensor", "achieved": round(achieved, 1),
+                "peak": peak, "unit": "TFLOP/s", "frac": round(achieved / peak, 3),
+                "peak_source": f"{src} bf16 sustained (kernel timed inside a long step)",
+                "flops_per_launch": round(gemm_flops / gemm_launches), "traffic": traffic,
+                "traffic_kernel": "gemm_fc1" if traffic else None}
+    ln = kernels.get("layernorm")
+    hbm = pk.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])
+    attn = kernels.get("attention")
+    out = {
+        "metric": "encoder images/s", "value": round(value, 1), "unit": "images/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic (seeded LCG: x N(0,1), weights N(0,0.02), zero biases, gamma 1, beta 0)",
+        "config": {"workload": "SigLIP-base 12-layer encoder forward (BASELINE config 5)", "global_batch": GLOBAL_BATCH,
+                   "per_gpu_batch": B, "seq_len": S, "d_model": D, "ffn": F, "heads": H, "layers": NLAYERS,
+                   "parallelism": f"dp{world}", "cuda_graph": graph is not None,
+                   "l2": "inputs larger than L2 (201 MB per activation tensor at B=512), no flush"},
+        "e2e": {"value": round(e2e_value, 1), "unit": "images/s", "h2d_bytes_per_step": M * D * 2,
+                "d2h_bytes_per_step": M * D * 2, "steps": e2e_steps},
+        "gpu_launches": args.steps * len(sched),
+        "roofline": roofline,
+        "kernels": kernels,
+        "gemm_tflops": round(achieved, 1),
+        "attention_tflops": attn["tflops"] if attn else None,
+        "rowop_gbs": ln["gbs"] if ln else None,
+        "rowop_frac_hbm": round(ln["gbs"] / hbm, 3) if ln else None,
+        "clocks": clock_info,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        out["cpu_baseline"] = cpu_baseline(args.cpu_images)
+    if world > 1:
+        import torch.distributed as dist
+        del graph
+        dist.destroy_process_group()
+    return out if rank == 0 else None
+
+
+# ---- the CPU leg: the reference's numpy layer (oracle port) ------------------------------------------------------------
+def cpu_layer_setup(seed: int = 3):
+    import numpy as np
+    from oracle import lcg, siglip
+    x = lcg.normal_fp16(S, D, seed)
+    p = siglip.baseline_layer_params(D, F, 1)
+    return np, siglip, x, p
+
+
+def cpu_baseline(images: int) -> dict:
+    np, siglip, x, p = cpu_layer_setup()
+    siglip.layer_reference_arrays(x, p, H)          # warm BLAS
+    t0 = time.perf_counter()
+    for _ in range(images):
+        cur = x
+        for _ in range(NLAYERS):
+            cur = siglip.layer_reference_arrays(cur, p, H)["OUT"]
+    dt = time.perf_counter() - t0
+    return {"value": round(images / dt, 4), "unit": "images/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"{images} image(s) x {NLAYERS} layers (S={S}, D={D}) of the 512-image batch through the numpy "
+                      f"oracle of siglip_ref.layer_reference (fp32 BLAS, all host threads); {dt:.1f} s"}
+
+
+def run_reference(args, rank: int, world: int) -> dict | None:
+    if rank != 0:
+        return None
+    np, siglip, x, p = cpu_layer_setup()
+    for _ in range(max(0, args.warmup)):
+        siglip.layer_reference_arrays(x, p, H)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        siglip.layer_reference_arrays(x, p, H)
+        times.append(time.perf_counter() - t0)
+    t_layer = statistics.mean(times)
+    value = 1.0 / (NLAYERS * t_layer)
+    sample = (f"each step: 1 image through 1 of the {NLAYERS} layers (numpy fp32 oracle of siglip_ref, all host "
+              f"threads); images/s = 1 / ({NLAYERS} x mean layer time)")
+    return {"metric": "encoder images/s", "value": round(value, 4), "unit": "images/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t_layer * 1e3, 2),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded LCG)", "impl": "reference",
+            "config": {"workload": "SigLIP-base 12-layer encoder forward (BASELINE config 5)",
+                       "global_batch": GLOBAL_BATCH, "seq_len": S, "parallelism": "cpu"},
+            "cpu_baseline": {"value": round(value, 4), "unit": "images/s", "cores": os.cpu_count(), "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": round(value, 4), "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=40)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-images", type=int, default=2)
+    ap.add_argument("--debug", action="store_true")
+    args = ap.parse_args()
+    rank, world, local = dist_env()
+    if args.impl == "reference":
+        out = run_reference(args, rank, world)
+    else:
+        out = run_ours(args, rank, world, local)
+    if out is not None:
+        print(json.dumps(out), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -62,6 +62,12 @@ void sh_cuda_add_layernorm(uint64_t h, uint64_t y, uint64_t a, uint64_t b, uint6
 int sh_cuda_attention_batched(uint64_t q, uint64_t k, uint64_t v, uint64_t o, uint32_t S, uint32_t D, uint32_t H,
                               uint32_t ldq, uint32_t ldk, uint32_t ldv, uint32_t ldo, float scale, uint32_t B);
 
+/* ---- synthetic inputs -------------------------------------------------------------------------------------------
+ * N(mean, std) fp16 from the LCG of sh_test_fill_fp16: per element two draws d0, d1, u = (d + 0.5) / 2^24 and
+ * Box-Muller z = sqrt(-2 ln u0) cos(2 pi u1) in fp32, on the device. */
+void sh_cuda_fill_normal_fp16(uint64_t a, uint32_t rows, uint32_t cols, uint32_t ld, uint32_t seed, float mean,
+                              float stdev);
+
 #ifdef __cplusplus
 }
 #endif

@@ -55,6 +55,31 @@ __global__ void k_fill_lcg(__half *a, uint32_t rows, uint32_t cols, uint32_t ld,
     }
 }
 
+// N(mean, std): draw pair (d0, d1) -> u = (d + 0.5) / 2^24, z = sqrt(-2 ln u0) cos(2 pi u1) (Box-Muller), one pair
+// per element in row-major order; the same definition as the host generator of the test oracle, in fp32.
+__global__ void k_fill_normal(__half *a, uint32_t rows, uint32_t cols, uint32_t ld, uint32_t seed, float mean,
+                              float stdev) {
+    const uint64_t total = (uint64_t)rows * cols;
+    const uint64_t start = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) * kChunk;
+    if (start >= total) return;
+    const Affine j = lcg_jump(2 * start);
+    uint32_t s = j.a * (seed ^ kSeedXor) + j.c;
+    uint64_t r = start / cols, c = start - r * cols;
+    const uint64_t end = start + kChunk < total ? start + kChunk : total;
+    for (uint64_t i = start; i < end; ++i) {
+        s = s * kA + kC;
+        const float u0 = ((float)(s >> 8) + 0.5f) * (1.0f / 16777216.0f);
+        s = s * kA + kC;
+        const float u1 = ((float)(s >> 8) + 0.5f) * (1.0f / 16777216.0f);
+        const float z = sqrtf(-2.0f * logf(u0)) * cospif(2.0f * u1);
+        a[r * ld + c] = __float2half_rn(mean + stdev * z);
+        if (++c == cols) {
+            c = 0;
+            ++r;
+        }
+    }
+}
+
 __global__ void k_fill_parity(uint16_t *a, uint32_t rows, uint32_t cols, uint32_t ld, uint16_t even, uint16_t odd) {
     const uint64_t total = (uint64_t)rows * cols;
     for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < total; i += (uint64_t)gridDim.x * blockDim.x) {
@@ -95,6 +120,16 @@ void sh_test_fill_fp16(uint64_t a, uint32_t rows, uint32_t cols, uint32_t ld, ui
     const uint32_t grid = (uint32_t)((threads + 255) / 256);
     k_fill_lcg<<<grid, 256, 0, sh::stream()>>>((__half *)a, rows, cols, ld, seed, lo, (uint32_t)(hi - lo + 1), scale);
     sh::cuda_ok(cudaGetLastError(), "sh_test_fill_fp16");
+}
+
+void sh_cuda_fill_normal_fp16(uint64_t a, uint32_t rows, uint32_t cols, uint32_t ld, uint32_t seed, float mean,
+                              float stdev) {
+    if (rows == 0 || cols == 0) return;
+    const uint64_t total = (uint64_t)rows * cols;
+    const uint64_t threads = (total + kChunk - 1) / kChunk;
+    const uint32_t grid = (uint32_t)((threads + 255) / 256);
+    k_fill_normal<<<grid, 256, 0, sh::stream()>>>((__half *)a, rows, cols, ld, seed, mean, stdev);
+    sh::cuda_ok(cudaGetLastError(), "sh_cuda_fill_normal_fp16");
 }
 
 void sh_test_fill_int_fp16(uint64_t a, uint32_t rows, uint32_t cols, uint32_t ld, uint32_t seed, int lo, int hi) {

@@ -17,6 +17,7 @@ GEMM epilogues, so each intermediate is rounded to fp16 once instead of after ev
 from __future__ import annotations
 
 from dataclasses import dataclass, field
+from typing import Callable
 
 import numpy as np
 
@@ -76,35 +77,91 @@ def alloc_activations(rt: Runtime, B: int, S: int, D: int, F: int) -> Activation
                        ln2=a(M, D), g=a(M, F), out=a(M, D))
 
 
+def layer_ops(lib, act: Activations, w: LayerWeights, heads: int, eps: float, scale: float, x: int,
+              out: int) -> list[tuple[str, Callable[[], int]]]:
+    """The 7 library calls of one layer as (kind, enqueue) pairs; enqueue() returns the call's return code."""
+    B, S, D, F = act.B, act.S, act.D, act.F
+    M = B * S
+    A = L.SH_ALL
+
+    def ln1():
+        lib.sh_layernorm(act.ln1, x, w.g1, w.be1, M, D, D, eps, A)
+        return 0
+
+    def ln2():
+        lib.sh_layernorm(act.ln2, act.h, w.g2, w.be2, M, D, D, eps, A)
+        return 0
+
+    return [
+        ("layernorm", ln1),
+        ("gemm_qkv", lambda: lib.sh_cuda_gemm(act.ln1, w.wqkv, act.qkv, M, 3 * D, D, D, 3 * D, 3 * D, w.bqkv, 0, 0,
+                                              L.EPI_BIAS, 0)),
+        ("attention", lambda: lib.sh_cuda_attention_batched(act.qkv, act.qkv + 2 * D, act.qkv + 4 * D, act.o, S, D,
+                                                            heads, 3 * D, 3 * D, 3 * D, D, scale, B)),
+        ("gemm_o", lambda: lib.sh_cuda_gemm(act.o, w.wo, act.h, M, D, D, D, D, D, w.bo, x, D,
+                                            L.EPI_BIAS | L.EPI_RESIDUAL, 0)),
+        ("layernorm", ln2),
+        ("gemm_fc1", lambda: lib.sh_cuda_gemm(act.ln2, w.w1, act.g, M, F, D, D, F, F, w.b1, 0, 0,
+                                              L.EPI_BIAS | L.EPI_GELU, 0)),
+        ("gemm_fc2", lambda: lib.sh_cuda_gemm(act.g, w.w2, out, M, D, F, F, D, D, w.b2, act.h, D,
+                                              L.EPI_BIAS | L.EPI_RESIDUAL, 0)),
+    ]
+
+
+def op_work(kind: str, B: int, S: int, D: int, F: int, heads: int) -> tuple[float, float]:
+    """(algorithmic FLOPs, algorithmic HBM bytes) of one launch of `kind` (fp16 = 2 B per element)."""
+    M = B * S
+    if kind == "layernorm":
+        return 8.0 * M * D, 2.0 * (2 * M * D + 2 * D)
+    if kind == "gemm_qkv":
+        return 2.0 * M * D * 3 * D, 2.0 * (M * D + D * 3 * D + M * 3 * D + 3 * D)
+    if kind == "gemm_o":
+        return 2.0 * M * D * D, 2.0 * (M * D + D * D + 2 * M * D + D)
+    if kind == "gemm_fc1":
+        return 2.0 * M * D * F, 2.0 * (M * D + D * F + M * F + F)
+    if kind == "gemm_fc2":
+        return 2.0 * M * F * D, 2.0 * (M * F + F * D + 2 * M * D + D)
+    if kind == "attention":
+        return 4.0 * B * S * S * D, 2.0 * 4 * M * D
+    raise KeyError(kind)
+
+
 def layer_forward(lib, act: Activations, w: LayerWeights, heads: int, eps: float, scale: float,
                   x: int | None = None, out: int | None = None) -> int:
     """Enqueue one layer on the library stream: reads x (default act.x), writes out (default act.out).
-    Returns 0 or the first negative return code."""
-    B, S, D, F = act.B, act.S, act.D, act.F
-    M = B * S
+    Returns 0 or the first nonzero return code."""
     x = act.x if x is None else x
     out = act.out if out is None else out
-    A = L.SH_ALL
-    lib.sh_layernorm(act.ln1, x, w.g1, w.be1, M, D, D, eps, A)
-    rc = lib.sh_cuda_gemm(act.ln1, w.wqkv, act.qkv, M, 3 * D, D, D, 3 * D, 3 * D, w.bqkv, 0, 0, L.EPI_BIAS, 0)
-    rc = rc or lib.sh_cuda_attention_batched(act.qkv, act.qkv + 2 * D, act.qkv + 4 * D, act.o, S, D, heads,
-                                             3 * D, 3 * D, 3 * D, D, scale, B)
-    rc = rc or lib.sh_cuda_gemm(act.o, w.wo, act.h, M, D, D, D, D, D, w.bo, x, D, L.EPI_BIAS | L.EPI_RESIDUAL, 0)
-    lib.sh_layernorm(act.ln2, act.h, w.g2, w.be2, M, D, D, eps, A)
-    rc = rc or lib.sh_cuda_gemm(act.ln2, w.w1, act.g, M, F, D, D, F, F, w.b1, 0, 0, L.EPI_BIAS | L.EPI_GELU, 0)
-    rc = rc or lib.sh_cuda_gemm(act.g, w.w2, out, M, D, F, F, D, D, w.b2, act.h, D, L.EPI_BIAS | L.EPI_RESIDUAL, 0)
-    return rc
-
-
-def encoder_forward(lib, act: Activations, layers: list[LayerWeights], heads: int, eps: float, scale: float) -> int:
-    """All layers; the residual stream ping-pongs between act.x and act.out. Returns the address of the result."""
-    cur, nxt = act.x, act.out
-    for w in layers:
-        rc = layer_forward(lib, act, w, heads, eps, scale, x=cur, out=nxt)
+    for _, fn in layer_ops(lib, act, w, heads, eps, scale, x, out):
+        rc = fn()
         if rc:
-            raise RuntimeError(f"encoder layer failed with {rc}")
-        cur, nxt = nxt, cur
-    return cur
+            return rc
+    return 0
+
+
+def encoder_schedule(lib, act: Activations, layers: list[LayerWeights], heads: int, eps: float, scale: float,
+                     x_in: int | None = None) -> tuple[list[tuple[str, Callable[[], int]]], int]:
+    """Every call of a full forward pass and the address the result lands in. Layer 0 reads x_in (default act.x),
+    later layers ping-pong the residual stream between act.out and act.x, so x_in is never overwritten when it is a
+    separate buffer."""
+    cur = act.x if x_in is None else x_in
+    nxt = act.out
+    sched = []
+    for i, w in enumerate(layers):
+        sched += layer_ops(lib, act, w, heads, eps, scale, cur, nxt)
+        cur, nxt = nxt, (act.x if nxt == act.out else act.out)
+    return sched, cur
+
+
+def encoder_forward(lib, act: Activations, layers: list[LayerWeights], heads: int, eps: float, scale: float,
+                    x_in: int | None = None) -> int:
+    """All layers (see encoder_schedule). Returns the address of the result."""
+    sched, res = encoder_schedule(lib, act, layers, heads, eps, scale, x_in)
+    for kind, fn in sched:
+        rc = fn()
+        if rc:
+            raise RuntimeError(f"encoder {kind} failed with {rc}")
+    return res
 
 
 def launches_per_layer() -> int:
