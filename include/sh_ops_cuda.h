@@ -51,6 +51,18 @@ uint32_t sh_cuda_abi_version(void);                 /* 1 */
 int sh_cuda_gemm(uint64_t x, uint64_t w, uint64_t z, uint32_t M, uint32_t N, uint32_t K, uint32_t ldx, uint32_t ldw,
                  uint32_t ldz, uint64_t bias, uint64_t residual, uint32_t ldr, uint32_t flags, uint32_t splits);
 
+/* ---- split-K GEMM without allocation -------------------------------------------------------------------------
+ * No counterpart in the reference. The same computation, arguments and return codes as sh_cuda_gemm, for callers
+ * that cannot let the library call cudaMalloc (a host whose own pool owns all device memory, or a loop that cannot
+ * take cudaMalloc's implicit device synchronisation). Split-K partial tiles and arrival counters live in one fixed
+ * 8 MiB array compiled into the library (held on every GPU that loads it until exit) instead of a growable
+ * workspace; a call needing more (tiles x splits x 128 x BN x 4 bytes of partials, or more than 4096 tiles) returns
+ * -2. The first call on a device looks the array up with cudaGetSymbolAddress and should come before any stream
+ * capture. Calls share the array: calls that overlap on the GPU race and must be serialised by the caller. */
+int sh_cuda_gemm_splitk_noalloc(uint64_t x, uint64_t w, uint64_t z, uint32_t M, uint32_t N, uint32_t K, uint32_t ldx,
+                                uint32_t ldw, uint32_t ldz, uint64_t bias, uint64_t residual, uint32_t ldr,
+                                uint32_t flags, uint32_t splits);
+
 /* ---- fused residual add + LayerNorm ---------------------------------------------------------------------------
  * h = a + b (stored, fp16), y = layernorm(h) * gamma + beta, both rows x cols with leading dim ld. */
 void sh_cuda_add_layernorm(uint64_t h, uint64_t y, uint64_t a, uint64_t b, uint64_t gamma, uint64_t beta,

@@ -18,6 +18,8 @@
 // Shapes the TMA path cannot address (16-byte alignment of base or leading dimension) use a CUDA-core kernel.
 #include <string.h>
 
+#include <mutex>
+
 #include "sh_internal.cuh"
 
 namespace {
@@ -596,3 +598,138 @@ int sh_cuda_gemm(uint64_t x, uint64_t w, uint64_t z, uint32_t M, uint32_t N, uin
 }
 
 }  // extern "C"
+
+// ================================================================================================================
+// Split-K GEMM that allocates nothing: sh_cuda_gemm_splitk_noalloc.
+//
+// Some callers cannot let a library call cudaMalloc: hosts that hand every byte of device memory to their own pool
+// (a serving runtime with a fixed memory budget, a framework allocator that owns the device), and loops that cannot
+// afford cudaMalloc's implicit device-wide synchronisation. sh_cuda_gemm may grow its split-K workspace with
+// cudaMalloc on first use of a shape; this entry point instead uses one fixed scratch array compiled into the
+// library (kNoAllocScratchBytes = 8 MiB per device, which every GPU that loads the library holds until exit).
+// Layout: [arrival counters, 4096 x u32][error word][fp32 partial tiles]. The partial tiles of a call need
+// tiles x splits x 128 x BN x 4 bytes; a call that would need more than the array holds returns -2 and changes
+// nothing. The first call on a device looks up the array's device address with cudaGetSymbolAddress (with that
+// device current) and should therefore come before any stream capture on it. Every call shares the array and
+// clears the counters it uses before its kernel, on the caller's stream: calls that overlap on the GPU (two
+// streams, two threads) race on the array and must be serialised by the caller.
+// ================================================================================================================
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = 8u << 20;
+constexpr size_t kNoAllocCounters = 4096;
+constexpr size_t kNoAllocErrOffset = kNoAllocCounters * sizeof(uint32_t);
+constexpr size_t kNoAllocPartialOffset = 32768;
+static __device__ __align__(256) unsigned char g_splitk_scratch[kNoAllocScratchBytes];
+
+static void *g_scratch_addr[sh::kMaxDevices];
+static std::mutex g_scratch_mu;
+
+// Device address of g_splitk_scratch on `dev` (the current device); nullptr after printing the reason.
+void *noalloc_scratch(int dev) {
+    std::lock_guard<std::mutex> lk(g_scratch_mu);
+    if (!g_scratch_addr[dev]) {
+        void *p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_splitk_scratch);
+        if (e != cudaSuccess || !p) {
+            sh::set_error((int)e, "[sh_cuda_gemm_splitk_noalloc] cudaGetSymbolAddress failed: %s",
+                          cudaGetErrorString(e));
+            return nullptr;
+        }
+        g_scratch_addr[dev] = p;
+    }
+    return g_scratch_addr[dev];
+}
+
+}  // namespace
+
+extern "C" int sh_cuda_gemm_splitk_noalloc(uint64_t x, uint64_t w, uint64_t z, uint32_t M, uint32_t N, uint32_t K,
+                                           uint32_t ldx, uint32_t ldw, uint32_t ldz, uint64_t bias, uint64_t residual,
+                                           uint32_t ldr, uint32_t flags, uint32_t splits) {
+    const char *name = "sh_cuda_gemm_splitk_noalloc";
+    if (M == 0 || N == 0) return 0;
+    if (!x || !w || !z || ldx < K || ldw < N || ldz < N || ((flags & SH_EPI_BIAS) && !bias) ||
+        ((flags & SH_EPI_RESIDUAL) && (!residual || ldr < N))) {
+        sh::set_error(-1, "[%s] bad operands: %ux%ux%u ld %u/%u/%u", name, M, N, K, ldx, ldw, ldz);
+        return -1;
+    }
+    int dev = 0;
+    if (!sh::cuda_ok(cudaGetDevice(&dev), name)) return -1;
+    if (dev >= sh::kMaxDevices) {
+        sh::set_error(-1, "[%s] device %d out of range", name, dev);
+        return -1;
+    }
+    int num_sms = 0;
+    if (!sh::cuda_ok(cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev), name)) return -1;
+    int *bound_err = nullptr;
+    cudaStream_t st = sh::peek_stream(dev, &bound_err);
+    unsigned char *scratch = static_cast<unsigned char *>(noalloc_scratch(dev));
+    if (!scratch) return -1;
+
+    GemmArgs a;
+    memset(&a, 0, sizeof a);
+    a.z = (__half *)z;
+    a.bias = (const __half *)bias;
+    a.resid = (const __half *)residual;
+    a.M = M;
+    a.N = N;
+    a.K = K;
+    a.ldz = ldz;
+    a.ldr = ldr;
+    a.flags = flags & (SH_EPI_ACCUMULATE | SH_EPI_BIAS | SH_EPI_GELU | SH_EPI_RESIDUAL);
+    a.err = bound_err ? bound_err : reinterpret_cast<int *>(scratch + kNoAllocErrOffset);
+    a.vec = sh::aligned16(z) && ldz % 8 == 0 && (!(flags & SH_EPI_BIAS) || sh::aligned16(bias)) &&
+            (!(flags & SH_EPI_RESIDUAL) || (sh::aligned16(residual) && ldr % 8 == 0));
+    const bool tc = K > 0 && sh::aligned16(x) && sh::aligned16(w) && ldx % 8 == 0 && ldw % 8 == 0 &&
+                    sh::encode_tiled() != nullptr;
+    if (!tc) {   // the CUDA-core kernel needs no scratch
+        dim3 grid((N + 63) / 64, (M + 63) / 64);
+        if (grid.y > 65535u) {
+            sh::set_error(-1, "[%s] M = %u too large for the fallback kernel", name, M);
+            return -1;
+        }
+        k_gemm_simt<<<grid, 256, 0, st>>>((const __half *)x, (const __half *)w, ldx, ldw, a);
+        return sh::cuda_ok(cudaGetLastError(), name) ? 0 : -1;
+    }
+    Plan p = make_plan(M, N, K, splits, num_sms);
+    a.tiles_n = p.tiles_n;
+    a.num_tiles = p.tiles_m * p.tiles_n;
+    a.k_blocks = p.k_blocks;
+    a.splits = p.splits;
+    a.kb_per_split = p.kb_per_split;
+    if (p.splits > 1) {
+        const size_t need = (size_t)a.num_tiles * p.splits * BM * p.bn * sizeof(float);
+        if (a.num_tiles > kNoAllocCounters || need > kNoAllocScratchBytes - kNoAllocPartialOffset) {
+            sh::set_error(-2, "[%s] %ux%ux%u in %u splits needs %zu B of partial tiles for %u tiles; the fixed scratch "
+                          "holds %zu B and %zu tiles", name, M, N, K, p.splits, need, a.num_tiles,
+                          kNoAllocScratchBytes - kNoAllocPartialOffset, kNoAllocCounters);
+            return -2;
+        }
+        a.counters = reinterpret_cast<uint32_t *>(scratch);
+        a.ws = reinterpret_cast<float *>(scratch + kNoAllocPartialOffset);
+        // the arrival counters this call uses must start at zero (a call that gave up may have left them set)
+        if (!sh::cuda_ok(cudaMemsetAsync(a.counters, 0, a.num_tiles * sizeof(uint32_t), st), name)) return -1;
+    }
+    CUtensorMap mx, mw;
+    if (!sh::make_map_2d(&mx, (const void *)x, M, K, ldx, BM, BK, true) ||
+        !sh::make_map_2d(&mw, (const void *)w, K, N, ldw, BK, 64, true)) {
+        sh::set_error(-1, "[%s] cuTensorMapEncodeTiled failed for %ux%ux%u", name, M, N, K);
+        return -1;
+    }
+    const uint32_t grid = min(a.num_tiles * p.splits, (uint32_t)num_sms);
+    switch (p.bn) {
+        case 256:
+            if (!set_smem_attr<256>()) return -1;
+            k_gemm_tc<256><<<grid, kThreads, TileCfg<256>::kSmem, st>>>(mx, mw, a);
+            break;
+        case 128:
+            if (!set_smem_attr<128>()) return -1;
+            k_gemm_tc<128><<<grid, kThreads, TileCfg<128>::kSmem, st>>>(mx, mw, a);
+            break;
+        default:
+            if (!set_smem_attr<64>()) return -1;
+            k_gemm_tc<64><<<grid, kThreads, TileCfg<64>::kSmem, st>>>(mx, mw, a);
+            break;
+    }
+    return sh::cuda_ok(cudaGetLastError(), name) ? 0 : -1;
+}

@@ -48,6 +48,9 @@ int current_device();
 void set_error(int code, const char *fmt, ...);   // record + print "[sh_...] ..." once per call
 bool cuda_ok(cudaError_t e, const char *where);   // record a CUDA failure, returns e == cudaSuccess
 inline cudaStream_t stream() { return state().stream; }
+// The stream bound with sh_cuda_set_stream and the kernels' error word, if the device's state already exists;
+// never initialises it (so never allocates). nullptr / the legacy default stream otherwise.
+cudaStream_t peek_stream(int device, int **dev_err);
 float *workspace(size_t bytes);       // grows the split-K workspace (not during stream capture)
 uint32_t *tile_counters(size_t n);
 

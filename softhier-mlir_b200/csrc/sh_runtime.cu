@@ -123,6 +123,15 @@ uint32_t *tile_counters(size_t n) {
     return s.counters;
 }
 
+cudaStream_t peek_stream(int device, int **dev_err) {
+    if (device < 0 || device >= kMaxDevices || !g_state[device].ready) {
+        *dev_err = nullptr;
+        return nullptr;
+    }
+    *dev_err = g_state[device].dev_err;
+    return g_state[device].stream;
+}
+
 PFN_encodeTiled encode_tiled() {
     static PFN_encodeTiled fn = nullptr;
     static bool tried = false;

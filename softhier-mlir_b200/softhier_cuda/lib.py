@@ -76,6 +76,7 @@ SIGNATURES: dict[str, tuple] = {
     "sh_cuda_add_layernorm": (None, [u64, u64, u64, u64, u64, u64, u32, u32, u32, f32]),
     "sh_cuda_attention_batched": (i32, [u64, u64, u64, u64, u32, u32, u32, u32, u32, u32, u32, f32, u32]),
     "sh_cuda_fill_normal_fp16": (None, [u64, u32, u32, u32, u32, f32, f32]),
+    "sh_cuda_gemm_splitk_noalloc": (i32, [u64, u64, u64, u32, u32, u32, u32, u32, u32, u64, u64, u32, u32, u32]),
 }
 
 # sh_ops_cuda.h constants
