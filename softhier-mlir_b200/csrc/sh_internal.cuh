@@ -65,6 +65,10 @@ PFN_encodeTiled encode_tiled();
 // 2-D fp16 row-major tensor [rows, cols] (leading dim ld elements), box [box_rows, box_cols], 128-B swizzle.
 bool make_map_2d(CUtensorMap *m, const void *base, uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_rows,
                  uint32_t box_cols, bool swizzle128);
+// 3-D fp16 tensor [batches, rows, cols]: row stride ld elements, batch stride batch_ld elements, box
+// [1, box_rows, box_cols], 128-byte swizzle. Rows past `rows` inside a batch read as zeros.
+bool make_map_3d(CUtensorMap *m, const void *base, uint64_t batches, uint64_t rows, uint64_t cols, uint64_t ld,
+                 uint64_t batch_ld, uint32_t box_rows, uint32_t box_cols);
 
 inline bool aligned16(uint64_t p) { return (p & 15u) == 0; }
 
@@ -133,6 +137,20 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *m, uin
             smem_u32(dst)),
         "l"(reinterpret_cast<uint64_t>(m)), "r"(smem_u32(bar)), "r"(x), "r"(y)
         : "memory");
+}
+
+// 3-D TMA tile load (x innermost).
+__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *m, uint64_t *bar, int32_t x, int32_t y,
+                                            int32_t z) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::
+            "r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(m)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
+        : "memory");
+}
+// Make this thread's generic-proxy shared-memory writes visible to the async proxy (TMA / tensor cores).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
 // ---- tcgen05: tensor memory + UMMA ----------------------------------------------------------
