@@ -26,7 +26,8 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BK = 64;
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;   // warp 0 TMA, warp 1 MMA, warps 2..9 epilogue
+constexpr uint32_t kEpiWarps = 8;
 
 template <int BN>
 struct TileCfg {
@@ -95,7 +96,7 @@ __device__ __forceinline__ void epilogue8(const GemmArgs &a, uint32_t row, uint3
         }
         if (f & SH_EPI_GELU) {
 #pragma unroll
-            for (int i = 0; i < 8; ++i) v[i] = gelu_tanh(v[i]);
+            for (int i = 0; i < 8; ++i) v[i] = gelu_fast(v[i]);
         }
         if (f & SH_EPI_RESIDUAL) {
             uint4 raw = *reinterpret_cast<const uint4 *>(a.resid + (size_t)row * a.ldr + col);
@@ -120,10 +121,56 @@ __device__ __forceinline__ void epilogue8(const GemmArgs &a, uint32_t row, uint3
             float t = v[i];
             if (f & SH_EPI_ACCUMULATE) t += __half2float(zp[i]);
             if (f & SH_EPI_BIAS) t += __half2float(a.bias[c]);
-            if (f & SH_EPI_GELU) t = gelu_tanh(t);
+            if (f & SH_EPI_GELU) t = gelu_fast(t);
             if (f & SH_EPI_RESIDUAL) t += __half2float(a.resid[(size_t)row * a.ldr + c]);
             zp[i] = __float2half_rn(t);
         }
+    }
+}
+
+__device__ __forceinline__ void load32(const __half *p, uint4 (&d)[4]) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) d[i] = *reinterpret_cast<const uint4 *>(p + 8 * i);
+}
+__device__ __forceinline__ void add8(float *v, const uint4 &raw) {
+    const __half2 *h = reinterpret_cast<const __half2 *>(&raw);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float2 t = __half22float2(h[i]);
+        v[2 * i] += t.x;
+        v[2 * i + 1] += t.y;
+    }
+}
+// fused epilogue of 32 consecutive in-range columns of one row on the 16-byte path; `res` holds the residual
+__device__ __forceinline__ void epilogue32(const GemmArgs &a, uint32_t row, uint32_t col, float (&v)[32],
+                                           const uint4 (&res)[4]) {
+    const uint32_t f = a.flags;
+    __half *zp = a.z + (size_t)row * a.ldz + col;
+    if (f & SH_EPI_ACCUMULATE) {
+        uint4 old[4];
+        load32(zp, old);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) add8(v + 8 * q, old[q]);
+    }
+    if (f & SH_EPI_BIAS) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) add8(v + 8 * q, __ldg(reinterpret_cast<const uint4 *>(a.bias + col + 8 * q)));
+    }
+    if (f & SH_EPI_GELU) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = gelu_fast(v[i]);
+    }
+    if (f & SH_EPI_RESIDUAL) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) add8(v + 8 * q, res[q]);
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        uint4 out;
+        __half2 *o = reinterpret_cast<__half2 *>(&out);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) o[i] = __floats2half2_rn(v[8 * q + 2 * i], v[8 * q + 2 * i + 1]);
+        *reinterpret_cast<uint4 *>(zp + 8 * q) = out;
     }
 }
 
@@ -153,9 +200,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&tfull[i], 1);
-            mbar_init(&tempty[i], 4);
+            mbar_init(&tempty[i], kEpiWarps);
         }
-        mbar_init(esync, 4);
+        mbar_init(esync, kEpiWarps);
         mbar_init(mdone, 1);
         *abort = 0;
         fence_mbar_init();
@@ -252,21 +299,31 @@ __global__ void __launch_bounds__(kThreads, 1)
             drain_wait(mdone, 0);
         }
     } else {
-        // ---------------- epilogue (warps 2..5) ----------------
-        const uint32_t quarter = warp & 3u;   // TMEM lanes [32 quarter, 32 quarter + 32)
+        // ---------------- epilogue (warps 2..9) ----------------
+        // warp w drains TMEM lane quarter (w % 4) = 32 rows, column half (w - 2) / 4 of the tile
+        const uint32_t quarter = warp & 3u;
+        const uint32_t half = (warp - 2u) >> 2;
+        constexpr uint32_t HB = BN / 2;            // columns per warp
         const uint32_t row_in_tile = quarter * 32 + lane;
+        const bool want_res = (a.flags & SH_EPI_RESIDUAL) != 0;
         uint32_t acc = 0, acc_phase = 0, es_phase = 0;
         for (uint32_t u = blockIdx.x; u < total_units; u += gridDim.x) {
             const uint32_t tile = u / a.splits, split = u - tile * a.splits;
             const uint32_t tm = tile / a.tiles_n, tn = tile - tm * a.tiles_n;
+            const uint32_t row = tm * BM + row_in_tile;
+            const uint32_t col0 = tn * BN + half * HB;
+            // residual of the first chunk is fetched before the accumulator is ready
+            uint4 res[4] = {};
+            const bool res_vec = want_res && a.vec && row < a.M;
+            if (res_vec && a.splits == 1 && col0 + 32 <= a.N) load32(a.resid + (size_t)row * a.ldr + col0, res);
             if (!mbar_wait(&tfull[acc], acc_phase, abort, a.err)) break;
             tc_fence_after();
-            const uint32_t row = tm * BM + row_in_tile;
-            const uint32_t taddr = tmem_base + ((quarter * 32u) << 16) + acc * BN;
-            float *part = a.splits > 1 ? a.ws + ((size_t)tile * a.splits + split) * (BM * BN) + (size_t)row_in_tile * BN
+            const uint32_t taddr = tmem_base + ((quarter * 32u) << 16) + acc * BN + half * HB;
+            float *part = a.splits > 1 ? a.ws + ((size_t)tile * a.splits + split) * (BM * BN) +
+                                             (size_t)row_in_tile * BN + half * HB
                                        : nullptr;
 #pragma unroll 1
-            for (int c = 0; c < BN / 32; ++c) {
+            for (uint32_t c = 0; c < HB / 32; ++c) {
                 uint32_t r[32];
                 tmem_ld_32x32b_x32(taddr + c * 32, r);
                 tmem_ld_wait();
@@ -276,15 +333,28 @@ __global__ void __launch_bounds__(kThreads, 1)
                         reinterpret_cast<float4 *>(part + c * 32)[i] =
                             make_float4(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]),
                                         __uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3]));
+                    continue;
+                }
+                const uint32_t col = col0 + c * 32;
+                uint4 nres[4] = {};
+                if (res_vec && c + 1 < HB / 32 && col + 64 <= a.N)
+                    load32(a.resid + (size_t)row * a.ldr + col + 32, nres);   // next chunk's residual in flight
+                float v[32];
+#pragma unroll
+                for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+                if (a.vec && row < a.M && col + 32 <= a.N) {
+                    epilogue32(a, row, col, v, res);
                 } else {
 #pragma unroll
                     for (int g = 0; g < 4; ++g) {
-                        float v[8];
+                        float w8[8];
 #pragma unroll
-                        for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[8 * g + i]);
-                        epilogue8(a, row, tn * BN + c * 32 + g * 8, v);
+                        for (int i = 0; i < 8; ++i) w8[i] = v[8 * g + i];
+                        epilogue8(a, row, col + g * 8, w8);
                     }
                 }
+#pragma unroll
+                for (int i = 0; i < 4; ++i) res[i] = nres[i];
             }
             tc_fence_before();
             __syncwarp();
@@ -305,9 +375,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (!epi_sync(esync, es_phase, abort, a.err)) break;
                 if (*last_flag) {
                     __threadfence();
-                    const float *base = a.ws + (size_t)tile * a.splits * (BM * BN) + (size_t)row_in_tile * BN;
+                    const float *base =
+                        a.ws + (size_t)tile * a.splits * (BM * BN) + (size_t)row_in_tile * BN + half * HB;
 #pragma unroll 1
-                    for (int c = 0; c < BN / 8; ++c) {
+                    for (uint32_t c = 0; c < HB / 8; ++c) {
                         float v[8] = {0, 0, 0, 0, 0, 0, 0, 0};
                         for (uint32_t s = 0; s < a.splits; ++s) {
                             const float4 *p = reinterpret_cast<const float4 *>(base + (size_t)s * (BM * BN) + c * 8);
@@ -315,7 +386,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                             v[0] += p0.x; v[1] += p0.y; v[2] += p0.z; v[3] += p0.w;
                             v[4] += p1.x; v[5] += p1.y; v[6] += p1.z; v[7] += p1.w;
                         }
-                        epilogue8(a, row, tn * BN + c * 8, v);
+                        epilogue8(a, row, col0 + c * 8, v);
                     }
                 }
                 // last_flag is rewritten for the next tile only after every warp has read it

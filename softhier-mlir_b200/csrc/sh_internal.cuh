@@ -215,6 +215,16 @@ __host__ __device__ constexpr uint32_t umma_idesc_f16(uint32_t M, uint32_t N, ui
     return (1u << 4) | (a_mn_major << 15) | (b_mn_major << 16) | ((N >> 3) << 17) | ((M >> 4) << 24);
 }
 
+// tanh-GELU 0.5 x (1 + tanh(u)), u = sqrt(2/pi) (x + 0.044715 x^3), with the hardware tanh.approx.f32 (relative
+// error about 2^-11, the precision of the fp16 result the epilogue stores).
+__device__ __forceinline__ float gelu_fast(float x) {
+    const float u = 0.7978845608028654f * fmaf(0.044715f * x, x * x, x);
+    float t;
+    asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(u));
+    const float hx = 0.5f * x;
+    return fmaf(hx, t, hx);
+}
+
 __device__ __forceinline__ float gelu_tanh(float x) {
     // 0.5 x (1 + tanh(u)) with u = sqrt(2/pi) (x + 0.044715 x^3), written as x * sigmoid(2u)
     const float u2 = 1.5957691216057308f * (x + 0.044715f * x * x * x);
