@@ -80,46 +80,46 @@ builtin.module {
     softhier.hbm_fill_lcg %be21 {seed = 117 : i32, lo = -4 : i32, hi = 4 : i32, scale = 0.125 : f32} : memref<1x128xf16, "hbm_west">
     softhier.mark {tag = "start"}
     softhier.layernorm %x, %g10, %be10 -> %ln1 {eps = 1.0e-6 : f32, cluster = -1 : i32} : memref<64x128xf16, "hbm_west">, memref<1x128xf16, "hbm_west">, memref<1x128xf16, "hbm_west"> -> memref<64x128xf16, "hbm_west">
-    softhier.gemm %ln1, %wq0 into %q {fmt = "fp16", tile_m = 256 : i32, tile_n = 256 : i32, tile_k = 256 : i32, pipeline, cluster = -1 : i32} : memref<64x128xf16, "hbm_west">, memref<128x128xf16, "hbm_west">, memref<64x128xf16, "hbm_west">
+    softhier.gemm %ln1, %wq0 into %q {fmt = "fp16", tile_m = 64 : i32, tile_n = 64 : i32, tile_k = 64 : i32, pipeline, cluster = -1 : i32} : memref<64x128xf16, "hbm_west">, memref<128x128xf16, "hbm_west">, memref<64x128xf16, "hbm_west">
     softhier.add_bias %q, %bq0 -> %q {cluster = -1 : i32} : memref<64x128xf16, "hbm_west">, memref<1x128xf16, "hbm_west"> -> memref<64x128xf16, "hbm_west">
-    softhier.gemm %ln1, %wk0 into %k {fmt = "fp16", tile_m = 256 : i32, tile_n = 256 : i32, tile_k = 256 : i32, pipeline, cluster = -1 : i32} : memref<64x128xf16, "hbm_west">, memref<128x128xf16, "hbm_west">, memref<64x128xf16, "hbm_west">
+    softhier.gemm %ln1, %wk0 into %k {fmt = "fp16", tile_m = 64 : i32, tile_n = 64 : i32, tile_k = 64 : i32, pipeline, cluster = -1 : i32} : memref<64x128xf16, "hbm_west">, memref<128x128xf16, "hbm_west">, memref<64x128xf16, "hbm_west">
     softhier.add_bias %k, %bk0 -> %k {cluster = -1 : i32} : memref<64x128xf16, "hbm_west">, memref<1x128xf16, "hbm_west"> -> memref<64x128xf16, "hbm_west">
-    softhier.gemm %ln1, %wv0 into %v {fmt = "fp16", tile_m = 256 : i32, tile_n = 256 : i32, tile_k = 256 : i32, pipeline, cluster = -1 : i32} : memref<64x128xf16, "hbm_west">, memref<128x128xf16, "hbm_west">, memref<64x128xf16, "hbm_west">
+    softhier.gemm %ln1, %wv0 into %v {fmt = "fp16", tile_m = 64 : i32, tile_n = 64 : i32, tile_k = 64 : i32, pipeline, cluster = -1 : i32} : memref<64x128xf16, "hbm_west">, memref<128x128xf16, "hbm_west">, memref<64x128xf16, "hbm_west">
     softhier.add_bias %v, %bv0 -> %v {cluster = -1 : i32} : memref<64x128xf16, "hbm_west">, memref<1x128xf16, "hbm_west"> -> memref<64x128xf16, "hbm_west">
     softhier.mark {tag = "qkv0"}
     softhier.attention %q, %k, %v -> %o {scale = 0.125 : f32, heads = 2 : i32, q_block = 64 : i32, cluster = -1 : i32} : memref<64x128xf16, "hbm_west">, memref<64x128xf16, "hbm_west">, memref<64x128xf16, "hbm_west"> -> memref<64x128xf16, "hbm_west">
     softhier.group_barrier {grid_x = 4 : i32, grid_y = 4 : i32}
     softhier.mark {tag = "attn0"}
-    softhier.gemm %o, %wo0 into %ao {fmt = "fp16", tile_m = 256 : i32, tile_n = 256 : i32, tile_k = 256 : i32, pipeline, cluster = -1 : i32} : memref<64x128xf16, "hbm_west">, memref<128x128xf16, "hbm_west">, memref<64x128xf16, "hbm_west">
+    softhier.gemm %o, %wo0 into %ao {fmt = "fp16", tile_m = 64 : i32, tile_n = 64 : i32, tile_k = 64 : i32, pipeline, cluster = -1 : i32} : memref<64x128xf16, "hbm_west">, memref<128x128xf16, "hbm_west">, memref<64x128xf16, "hbm_west">
     softhier.add_bias %ao, %bo0 -> %ao {cluster = -1 : i32} : memref<64x128xf16, "hbm_west">, memref<1x128xf16, "hbm_west"> -> memref<64x128xf16, "hbm_west">
     softhier.add %x, %ao -> %h {cluster = -1 : i32} : memref<64x128xf16, "hbm_west">, memref<64x128xf16, "hbm_west"> -> memref<64x128xf16, "hbm_west">
     softhier.layernorm %h, %g20, %be20 -> %ln2 {eps = 1.0e-6 : f32, cluster = -1 : i32} : memref<64x128xf16, "hbm_west">, memref<1x128xf16, "hbm_west">, memref<1x128xf16, "hbm_west"> -> memref<64x128xf16, "hbm_west">
-    softhier.gemm %ln2, %w10 into %f1 {fmt = "fp16", tile_m = 256 : i32, tile_n = 256 : i32, tile_k = 256 : i32, pipeline, cluster = -1 : i32} : memref<64x128xf16, "hbm_west">, memref<128x256xf16, "hbm_west">, memref<64x256xf16, "hbm_west">
+    softhier.gemm %ln2, %w10 into %f1 {fmt = "fp16", tile_m = 64 : i32, tile_n = 64 : i32, tile_k = 64 : i32, pipeline, cluster = -1 : i32} : memref<64x128xf16, "hbm_west">, memref<128x256xf16, "hbm_west">, memref<64x256xf16, "hbm_west">
     softhier.add_bias %f1, %b10 -> %f1 {cluster = -1 : i32} : memref<64x256xf16, "hbm_west">, memref<1x256xf16, "hbm_west"> -> memref<64x256xf16, "hbm_west">
     softhier.gelu %f1 -> %g {cluster = -1 : i32} : memref<64x256xf16, "hbm_west"> -> memref<64x256xf16, "hbm_west">
-    softhier.gemm %g, %w20 into %f2 {fmt = "fp16", tile_m = 256 : i32, tile_n = 256 : i32, tile_k = 256 : i32, pipeline, cluster = -1 : i32} : memref<64x256xf16, "hbm_west">, memref<256x128xf16, "hbm_west">, memref<64x128xf16, "hbm_west">
+    softhier.gemm %g, %w20 into %f2 {fmt = "fp16", tile_m = 64 : i32, tile_n = 64 : i32, tile_k = 64 : i32, pipeline, cluster = -1 : i32} : memref<64x256xf16, "hbm_west">, memref<256x128xf16, "hbm_west">, memref<64x128xf16, "hbm_west">
     softhier.add_bias %f2, %b20 -> %f2 {cluster = -1 : i32} : memref<64x128xf16, "hbm_west">, memref<1x128xf16, "hbm_west"> -> memref<64x128xf16, "hbm_west">
     softhier.add %h, %f2 -> %out {cluster = -1 : i32} : memref<64x128xf16, "hbm_west">, memref<64x128xf16, "hbm_west"> -> memref<64x128xf16, "hbm_west">
     softhier.mark {tag = "layer0"}
     softhier.layernorm %out, %g11, %be11 -> %ln1 {eps = 1.0e-6 : f32, cluster = -1 : i32} : memref<64x128xf16, "hbm_west">, memref<1x128xf16, "hbm_west">, memref<1x128xf16, "hbm_west"> -> memref<64x128xf16, "hbm_west">
-    softhier.gemm %ln1, %wq1 into %q {fmt = "fp16", tile_m = 256 : i32, tile_n = 256 : i32, tile_k = 256 : i32, pipeline, cluster = -1 : i32} : memref<64x128xf16, "hbm_west">, memref<128x128xf16, "hbm_west">, memref<64x128xf16, "hbm_west">
+    softhier.gemm %ln1, %wq1 into %q {fmt = "fp16", tile_m = 64 : i32, tile_n = 64 : i32, tile_k = 64 : i32, pipeline, cluster = -1 : i32} : memref<64x128xf16, "hbm_west">, memref<128x128xf16, "hbm_west">, memref<64x128xf16, "hbm_west">
     softhier.add_bias %q, %bq1 -> %q {cluster = -1 : i32} : memref<64x128xf16, "hbm_west">, memref<1x128xf16, "hbm_west"> -> memref<64x128xf16, "hbm_west">
-    softhier.gemm %ln1, %wk1 into %k {fmt = "fp16", tile_m = 256 : i32, tile_n = 256 : i32, tile_k = 256 : i32, pipeline, cluster = -1 : i32} : memref<64x128xf16, "hbm_west">, memref<128x128xf16, "hbm_west">, memref<64x128xf16, "hbm_west">
+    softhier.gemm %ln1, %wk1 into %k {fmt = "fp16", tile_m = 64 : i32, tile_n = 64 : i32, tile_k = 64 : i32, pipeline, cluster = -1 : i32} : memref<64x128xf16, "hbm_west">, memref<128x128xf16, "hbm_west">, memref<64x128xf16, "hbm_west">
     softhier.add_bias %k, %bk1 -> %k {cluster = -1 : i32} : memref<64x128xf16, "hbm_west">, memref<1x128xf16, "hbm_west"> -> memref<64x128xf16, "hbm_west">
-    softhier.gemm %ln1, %wv1 into %v {fmt = "fp16", tile_m = 256 : i32, tile_n = 256 : i32, tile_k = 256 : i32, pipeline, cluster = -1 : i32} : memref<64x128xf16, "hbm_west">, memref<128x128xf16, "hbm_west">, memref<64x128xf16, "hbm_west">
+    softhier.gemm %ln1, %wv1 into %v {fmt = "fp16", tile_m = 64 : i32, tile_n = 64 : i32, tile_k = 64 : i32, pipeline, cluster = -1 : i32} : memref<64x128xf16, "hbm_west">, memref<128x128xf16, "hbm_west">, memref<64x128xf16, "hbm_west">
     softhier.add_bias %v, %bv1 -> %v {cluster = -1 : i32} : memref<64x128xf16, "hbm_west">, memref<1x128xf16, "hbm_west"> -> memref<64x128xf16, "hbm_west">
     softhier.mark {tag = "qkv1"}
     softhier.attention %q, %k, %v -> %o {scale = 0.125 : f32, heads = 2 : i32, q_block = 64 : i32, cluster = -1 : i32} : memref<64x128xf16, "hbm_west">, memref<64x128xf16, "hbm_west">, memref<64x128xf16, "hbm_west"> -> memref<64x128xf16, "hbm_west">
     softhier.group_barrier {grid_x = 4 : i32, grid_y = 4 : i32}
     softhier.mark {tag = "attn1"}
-    softhier.gemm %o, %wo1 into %ao {fmt = "fp16", tile_m = 256 : i32, tile_n = 256 : i32, tile_k = 256 : i32, pipeline, cluster = -1 : i32} : memref<64x128xf16, "hbm_west">, memref<128x128xf16, "hbm_west">, memref<64x128xf16, "hbm_west">
+    softhier.gemm %o, %wo1 into %ao {fmt = "fp16", tile_m = 64 : i32, tile_n = 64 : i32, tile_k = 64 : i32, pipeline, cluster = -1 : i32} : memref<64x128xf16, "hbm_west">, memref<128x128xf16, "hbm_west">, memref<64x128xf16, "hbm_west">
     softhier.add_bias %ao, %bo1 -> %ao {cluster = -1 : i32} : memref<64x128xf16, "hbm_west">, memref<1x128xf16, "hbm_west"> -> memref<64x128xf16, "hbm_west">
     softhier.add %out, %ao -> %h {cluster = -1 : i32} : memref<64x128xf16, "hbm_west">, memref<64x128xf16, "hbm_west"> -> memref<64x128xf16, "hbm_west">
     softhier.layernorm %h, %g21, %be21 -> %ln2 {eps = 1.0e-6 : f32, cluster = -1 : i32} : memref<64x128xf16, "hbm_west">, memref<1x128xf16, "hbm_west">, memref<1x128xf16, "hbm_west"> -> memref<64x128xf16, "hbm_west">
-    softhier.gemm %ln2, %w11 into %f1 {fmt = "fp16", tile_m = 256 : i32, tile_n = 256 : i32, tile_k = 256 : i32, pipeline, cluster = -1 : i32} : memref<64x128xf16, "hbm_west">, memref<128x256xf16, "hbm_west">, memref<64x256xf16, "hbm_west">
+    softhier.gemm %ln2, %w11 into %f1 {fmt = "fp16", tile_m = 64 : i32, tile_n = 64 : i32, tile_k = 64 : i32, pipeline, cluster = -1 : i32} : memref<64x128xf16, "hbm_west">, memref<128x256xf16, "hbm_west">, memref<64x256xf16, "hbm_west">
     softhier.add_bias %f1, %b11 -> %f1 {cluster = -1 : i32} : memref<64x256xf16, "hbm_west">, memref<1x256xf16, "hbm_west"> -> memref<64x256xf16, "hbm_west">
     softhier.gelu %f1 -> %g {cluster = -1 : i32} : memref<64x256xf16, "hbm_west"> -> memref<64x256xf16, "hbm_west">
-    softhier.gemm %g, %w21 into %f2 {fmt = "fp16", tile_m = 256 : i32, tile_n = 256 : i32, tile_k = 256 : i32, pipeline, cluster = -1 : i32} : memref<64x256xf16, "hbm_west">, memref<256x128xf16, "hbm_west">, memref<64x128xf16, "hbm_west">
+    softhier.gemm %g, %w21 into %f2 {fmt = "fp16", tile_m = 64 : i32, tile_n = 64 : i32, tile_k = 64 : i32, pipeline, cluster = -1 : i32} : memref<64x256xf16, "hbm_west">, memref<256x128xf16, "hbm_west">, memref<64x128xf16, "hbm_west">
     softhier.add_bias %f2, %b21 -> %f2 {cluster = -1 : i32} : memref<64x128xf16, "hbm_west">, memref<1x128xf16, "hbm_west"> -> memref<64x128xf16, "hbm_west">
     softhier.add %h, %f2 -> %out {cluster = -1 : i32} : memref<64x128xf16, "hbm_west">, memref<64x128xf16, "hbm_west"> -> memref<64x128xf16, "hbm_west">
     softhier.mark {tag = "layer1"}
