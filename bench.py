@@ -392,6 +392,183 @@ def run_reference(args, rank: int, world: int) -> dict | None:
             "e2e": {"value": round(value, 4), "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
+# ---- secondary workloads (BASELINE configs 1 and 2): their own JSON lines, not the headline ------------------------
+def _event_time(torch, stream, fn, steps: int) -> float:
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        fn()
+    e1.record(stream)
+    e1.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
+def run_gemm512(args, local: int) -> dict:
+    """Config 1: Z = X W, 512^3, X / W uniform [-1, 1) from the LCG. Per-call latency (eager) and throughput of
+    1000 back-to-back calls replayed from a CUDA graph."""
+    import torch
+    from softhier_cuda import lib as L
+    from softhier_cuda.runtime import Runtime
+    rt = Runtime.open(local, arena_bytes=64 << 20)
+    lib = rt.lib
+    n = 512
+    x, w, z = rt.alloc(n, n), rt.alloc(n, n), rt.alloc(n, n)
+    lib.sh_test_fill_fp16(x, n, n, n, 1, -1024, 1023, 1.0 / 1024)
+    lib.sh_test_fill_fp16(w, n, n, n, 2, -1024, 1023, 1.0 / 1024)
+    stream = torch.cuda.Stream(device=local)
+    rt.activate(stream)
+    call = lambda: lib.sh_gemm(x, w, z, n, n, n, n, n, n, None, L.SH_ALL)  # noqa: E731
+    with torch.cuda.stream(stream):
+        for _ in range(max(3, args.warmup)):
+            call()
+    rt.check()
+    with torch.cuda.stream(stream):
+        lat = _event_time(torch, stream, call, max(10, args.steps))
+    g = torch.cuda.CUDAGraph()
+    reps = 1000
+    with torch.cuda.graph(g, stream=stream):
+        lib.sh_cuda_set_stream(torch.cuda.current_stream().cuda_stream)
+        for _ in range(reps):
+            call()
+    lib.sh_cuda_set_stream(stream.cuda_stream)
+    with torch.cuda.stream(stream):
+        g.replay()
+        thr = _event_time(torch, stream, g.replay, 3) / reps
+    rt.check()
+    flop = 2.0 * n ** 3
+    pk, src = peaks()
+    return {"metric": "GEMM 512^3 TFLOP/s", "value": round(flop / thr / 1e9, 2), "unit": "TFLOP/s", "n_gpus": 1,
+            "ms_per_call_graph": round(thr, 5), "ms_per_call_eager": round(lat, 5),
+            "latency_tflops": round(flop / lat / 1e9, 2), "frac_of_peak": round(flop / thr / 1e9 / pk["bf16_tflops"], 4),
+            "peak": f"{src} bf16 burst {pk['bf16_tflops']} TFLOP/s", "higher_is_better": True, "dtype": "f16",
+            "config": {"workload": "BASELINE config 1: 512^3 fp16 GEMM, fp32 accumulate",
+                       "note": "X, W, Z = 1.5 MB: L2-resident; 1000 calls per graph replay"}}
+
+
+def run_rowops(args, local: int) -> dict:
+    """Config 2 at the HBM-resident activation shape of config 5 (131072 rows x 768 / 3072): per-op GB/s, rotating
+    over buffers that total more than twice the L2 so every launch streams from HBM."""
+    import torch
+    from softhier_cuda import lib as L
+    from softhier_cuda.runtime import Runtime
+    rows = 131072
+    rt = Runtime.open(local, arena_bytes=(5 << 30))
+    lib = rt.lib
+    stream = torch.cuda.Stream(device=local)
+    out = {}
+    pk, src = peaks()
+    for cols in (768, 3072):
+        rt.reset()
+        nbuf = 2
+        xs = [rt.alloc(rows, cols) for _ in range(nbuf)]
+        bs = [rt.alloc(rows, cols) for _ in range(nbuf)]
+        ys = [rt.alloc(rows, cols) for _ in range(nbuf)]
+        g, be = rt.alloc(1, cols), rt.alloc(1, cols)
+        for i in range(nbuf):
+            lib.sh_cuda_fill_normal_fp16(xs[i], rows, cols, cols, 11 + i, 0.0, 1.0)
+            lib.sh_cuda_fill_normal_fp16(bs[i], rows, cols, cols, 21 + i, 0.0, 1.0)
+        lib.sh_cuda_fill_normal_fp16(g, 1, cols, cols, 13, 1.0, 0.02)
+        lib.sh_cuda_fill_normal_fp16(be, 1, cols, cols, 14, 0.0, 0.02)
+        rt.activate(stream)
+        A = L.SH_ALL
+        it = {"i": 0}
+
+        def nxt():
+            it["i"] = (it["i"] + 1) % nbuf
+            return it["i"]
+        ops = {
+            "layernorm": (lambda i: lib.sh_layernorm(ys[i], xs[i], g, be, rows, cols, cols, 1e-6, A), 2 * rows * cols * 2),
+            "softmax": (lambda i: lib.sh_softmax_rows(ys[i], xs[i], rows, cols, cols, 0.125, A), 2 * rows * cols * 2),
+            "gelu": (lambda i: lib.sh_gelu(ys[i], xs[i], rows, cols, cols, A), 2 * rows * cols * 2),
+            "add": (lambda i: lib.sh_add(ys[i], xs[i], bs[i], rows, cols, cols, A), 3 * rows * cols * 2),
+            "add_bias": (lambda i: lib.sh_add_bias(ys[i], xs[i], be, rows, cols, cols, A), 2 * rows * cols * 2),
+            "scale": (lambda i: lib.sh_scale(ys[i], xs[i], rows, cols, cols, 0.125, A), 2 * rows * cols * 2),
+            "transpose": (lambda i: lib.sh_transpose(ys[i], xs[i], rows, cols, cols, rows, A), 2 * rows * cols * 2),
+        }
+        with torch.cuda.stream(stream):
+            for name, (fn, nbytes) in ops.items():
+                for _ in range(3):
+                    fn(nxt())
+                ms = _event_time(torch, stream, lambda: fn(nxt()), max(10, args.steps))
+                out[f"{name}_{rows}x{cols}"] = {"ms": round(ms, 4), "gbs": round(nbytes / ms / 1e6, 1),
+                                                "frac_hbm": round(nbytes / ms / 1e6 / pk["hbm_gbs"], 3)}
+        rt.check()
+    worst = min(v["frac_hbm"] for v in out.values())
+    return {"metric": "row-op GB/s (HBM-resident)", "value": round(min(v["gbs"] for v in out.values()), 1),
+            "unit": "GB/s (slowest op)", "n_gpus": 1, "higher_is_better": True, "dtype": "f16", "ops": out,
+            "min_frac_hbm": worst, "peak": f"{src} copy {pk['hbm_gbs']} GB/s",
+            "config": {"workload": "BASELINE config 2 ops at 131072 x {768, 3072}",
+                       "l2": "2 rotating buffer sets of 201 / 805 MB per operand (> 2 x L2)"}}
+
+
+def run_summa(args, rank: int, world: int, local: int) -> dict | None:
+    """Config 4: C = A B, M = N = K = 16384, A / B uniform [-1, 1) from the LCG, block-distributed over the default
+    grid of the world size (1x1, 1x2, 2x2, 2x4). Panels of 2048 are pulled from their owners over NVLink by the copy
+    engines while the tcgen05 GEMM accumulates the previous panel. value = 2 n^3 / (max over ranks of the step
+    time)."""
+    import torch
+    from softhier_cuda import summa as SU
+    from softhier_cuda.runtime import Runtime
+    init_dist(world, local)
+    torch.cuda.set_device(local)
+    n = args.summa_n
+    pr, pc = SU.default_grid(world)
+    kb = n if world == 1 else min(2048, n // max(pr, pc))
+    lay = SU.Layout(n, n, n, pr, pc, kb)
+    rt = Runtime.open(local, arena_bytes=64 << 20)
+    if world > 1:
+        import torch.distributed as dist
+
+        def exchange(obj):
+            out = [None] * world
+            dist.all_gather_object(out, obj)
+            return out
+        bar = dist.barrier
+    else:
+        exchange, bar = (lambda x: [x]), (lambda: None)
+    compute, copy = torch.cuda.Stream(device=local), torch.cuda.Stream(device=local)
+    su = SU.SummaGPU(rt.lib, lay, rank, exchange, bar, (compute, copy))
+    su.fill_inputs(41, 42)
+    for _ in range(max(3, args.warmup)):
+        assert su.step(torch) == 0
+    torch.cuda.synchronize()
+    rt.check()
+    clocks = ClockSampler(local)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    clocks.start()
+    time.sleep(0.05)
+    steps = args.steps
+    e0.record(compute)
+    for _ in range(steps):
+        su.step(torch)
+    e1.record(compute)
+    e1.synchronize()
+    clock_info = clocks.stop()
+    barrier(world)
+    ms = max_over_ranks(e0.elapsed_time(e1) / steps, world)
+    rt.check()
+    su.close()
+    flop = 2.0 * n ** 3
+    pk, src = peaks()
+    tf = flop / ms / 1e9
+    peer_bytes = sum((lay.Mb * kb * 2 if p.a_rank != rank else 0) + (kb * lay.Nb * 2 if p.b_rank != rank else 0)
+                     for p in su.sched)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+    if rank != 0:
+        return None
+    return {"metric": "SUMMA 16384^3 TFLOP/s", "value": round(tf, 1), "unit": "TFLOP/s", "n_gpus": world,
+            "steps": steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
+            "scaling": "strong", "dtype": "f16", "frac_of_peak_per_gpu": round(tf / world / pk["bf16_tflops_sustained"], 3),
+            "peak": f"{src} bf16 sustained {pk['bf16_tflops_sustained']} TFLOP/s per GPU",
+            "peer_bytes_per_step_rank0": peer_bytes, "clocks": clock_info,
+            "config": {"workload": "BASELINE config 4: distributed SUMMA", "n": n, "grid": f"{pr}x{pc}", "panel": kb,
+                       "transport": "CUDA IPC + copy engines (cudaMemcpy2DAsync) over NVLink"}}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -402,10 +579,18 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-images", type=int, default=2)
     ap.add_argument("--debug", action="store_true")
+    ap.add_argument("--workload", choices=["encoder", "gemm512", "rowops", "summa"], default="encoder")
+    ap.add_argument("--summa-n", type=int, default=16384)
     args = ap.parse_args()
     rank, world, local = dist_env()
     if args.impl == "reference":
         out = run_reference(args, rank, world)
+    elif args.workload == "gemm512":
+        out = run_gemm512(args, local) if rank == 0 else None
+    elif args.workload == "rowops":
+        out = run_rowops(args, local) if rank == 0 else None
+    elif args.workload == "summa":
+        out = run_summa(args, rank, world, local)
     else:
         out = run_ours(args, rank, world, local)
     if out is not None:

@@ -40,6 +40,10 @@ uint32_t sh_cuda_abi_version(void);                 /* 1 */
  *   SH_EPI_BIAS        t = t + bias[col]         (bias: 1 x N fp16)
  *   SH_EPI_GELU        t = gelu_tanh(t)          (after the bias)
  *   SH_EPI_RESIDUAL    t = t + R[row, col]       (R: M x N fp16, leading dim ldr)
+ *   SH_EPI_F32_OUT     Z is fp32 (ldz in fp32 elements; SH_EPI_ACCUMULATE then reads fp32 Z)
+ *   SH_EPI_ACC_F32_IN  t = t + R32[row, col] with R32 an fp32 matrix passed as `residual` (leading dim ldr);
+ *                      not combined with SH_EPI_RESIDUAL. Together with SH_EPI_F32_OUT this carries a K-split
+ *                      product in fp32 across calls (the SUMMA panels) and rounds it to fp16 once.
  *   SH_GEMM_SIMT       use the CUDA-core fallback kernel (tests)
  * splits: 0 = library choice of split-K, 1 = none, n = K split n ways (partials reduced in a fixed order).
  * Returns 0 or -1 (reason printed). */
@@ -47,6 +51,8 @@ uint32_t sh_cuda_abi_version(void);                 /* 1 */
 #define SH_EPI_BIAS       0x2u
 #define SH_EPI_GELU       0x4u
 #define SH_EPI_RESIDUAL   0x8u
+#define SH_EPI_F32_OUT    0x10u
+#define SH_EPI_ACC_F32_IN 0x20u
 #define SH_GEMM_SIMT      0x100u
 int sh_cuda_gemm(uint64_t x, uint64_t w, uint64_t z, uint32_t M, uint32_t N, uint32_t K, uint32_t ldx, uint32_t ldw,
                  uint32_t ldz, uint64_t bias, uint64_t residual, uint32_t ldr, uint32_t flags, uint32_t splits);
@@ -79,6 +85,23 @@ int sh_cuda_attention_batched(uint64_t q, uint64_t k, uint64_t v, uint64_t o, ui
  * Box-Muller z = sqrt(-2 ln u0) cos(2 pi u1) in fp32, on the device. */
 void sh_cuda_fill_normal_fp16(uint64_t a, uint32_t rows, uint32_t cols, uint32_t ld, uint32_t seed, float mean,
                               float stdev);
+
+/* ---- LCG sub-block fill (2-D block-distributed inputs) -----------------------------------------------------------
+ * Fill rows x cols (leading dim ld) with elements [row0 .., col0 ..] of the global gcols-wide matrix that
+ * sh_test_fill_fp16(.., seed, lo, hi, scale) would produce: every rank generates exactly its own block. */
+void sh_cuda_fill_lcg_block(uint64_t a, uint32_t rows, uint32_t cols, uint32_t ld, uint32_t seed, int lo, int hi,
+                            float scale, uint64_t row0, uint64_t col0, uint64_t gcols);
+
+/* ---- peer memory for the multi-GPU SUMMA --------------------------------------------------------------------------
+ * Device buffers that other processes of the node can map (CUDA IPC), and asynchronous 2-D copies between any two
+ * device addresses of the node (copy engines over NVLink when source and destination are on different GPUs). */
+void *sh_cuda_ipc_alloc(size_t bytes);                     /* cudaMalloc'd, exportable; NULL on failure */
+int   sh_cuda_ipc_free(void *p);
+int   sh_cuda_ipc_handle(void *p, void *handle64);          /* 64-byte handle of a sh_cuda_ipc_alloc buffer */
+void *sh_cuda_ipc_open(const void *handle64);               /* map a peer's buffer into this process */
+int   sh_cuda_ipc_close(void *p);
+int   sh_cuda_copy2d(uint64_t dst, size_t dpitch, uint64_t src, size_t spitch, size_t width_bytes, size_t rows,
+                     void *stream);
 
 #ifdef __cplusplus
 }

@@ -349,7 +349,7 @@ __global__ void __launch_bounds__(160, 2)
                     if (c * 32 + i < valid) mb = fmaxf(mb, __uint_as_float(v[i]) * a.sl2);
             }
             const float mn = fmaxf(m, mb);
-            const float alpha = exp2f(m - mn);
+            const float alpha = fast_exp2(m - mn);
             // pass 2: p = 2^(s sl2 - mn) -> fp16 into the swizzled P tile; l accumulates the rounded values
             float ls = 0.f;
             uint8_t *prow = sp + r * 128;
@@ -362,8 +362,8 @@ __global__ void __launch_bounds__(160, 2)
 #pragma unroll
                 for (int i = 0; i < 16; ++i) {
                     const int k0 = c * 32 + 2 * i;
-                    const float p0 = (k0 < valid) ? exp2f(__uint_as_float(v[2 * i]) * a.sl2 - mn) : 0.f;
-                    const float p1 = (k0 + 1 < valid) ? exp2f(__uint_as_float(v[2 * i + 1]) * a.sl2 - mn) : 0.f;
+                    const float p0 = (k0 < valid) ? fast_exp2(__uint_as_float(v[2 * i]) * a.sl2 - mn) : 0.f;
+                    const float p1 = (k0 + 1 < valid) ? fast_exp2(__uint_as_float(v[2 * i + 1]) * a.sl2 - mn) : 0.f;
                     const __half2 hp = __floats2half2_rn(p0, p1);
                     const float2 back = __half22float2(hp);
                     ls += back.x + back.y;

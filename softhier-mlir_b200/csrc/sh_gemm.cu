@@ -68,21 +68,36 @@ __device__ __forceinline__ void drain_wait(uint64_t *bar, uint32_t parity) {
         if ((unsigned long long)(clock64() - t0) > SH_SPIN_CYCLES) break;
 }
 
-// fused epilogue of 8 consecutive columns of one row (values in v, fp32)
+// fused epilogue of 8 consecutive columns of one row (values in v, fp32). Z is fp16, or fp32 with SH_EPI_F32_OUT;
+// SH_EPI_ACC_F32_IN adds an fp32 matrix passed as `resid` (leading dim ldr) instead of an fp16 residual.
 __device__ __forceinline__ void epilogue8(const GemmArgs &a, uint32_t row, uint32_t col, float (&v)[8]) {
     if (row >= a.M || col >= a.N) return;
     const uint32_t f = a.flags;
+    const bool z32 = (f & SH_EPI_F32_OUT) != 0;
     __half *zp = a.z + (size_t)row * a.ldz + col;
+    float *zf = reinterpret_cast<float *>(a.z) + (size_t)row * a.ldz + col;
+    const float *rf = reinterpret_cast<const float *>(a.resid) + (size_t)row * a.ldr + col;
     if (a.vec && col + 8 <= a.N) {
         if (f & SH_EPI_ACCUMULATE) {
-            uint4 raw = *reinterpret_cast<const uint4 *>(zp);
-            const __half2 *h = reinterpret_cast<const __half2 *>(&raw);
+            if (z32) {
+                const float4 p0 = reinterpret_cast<const float4 *>(zf)[0], p1 = reinterpret_cast<const float4 *>(zf)[1];
+                v[0] += p0.x; v[1] += p0.y; v[2] += p0.z; v[3] += p0.w;
+                v[4] += p1.x; v[5] += p1.y; v[6] += p1.z; v[7] += p1.w;
+            } else {
+                uint4 raw = *reinterpret_cast<const uint4 *>(zp);
+                const __half2 *h = reinterpret_cast<const __half2 *>(&raw);
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                float2 t = __half22float2(h[i]);
-                v[2 * i] += t.x;
-                v[2 * i + 1] += t.y;
+                for (int i = 0; i < 4; ++i) {
+                    float2 t = __half22float2(h[i]);
+                    v[2 * i] += t.x;
+                    v[2 * i + 1] += t.y;
+                }
             }
+        }
+        if (f & SH_EPI_ACC_F32_IN) {
+            const float4 p0 = reinterpret_cast<const float4 *>(rf)[0], p1 = reinterpret_cast<const float4 *>(rf)[1];
+            v[0] += p0.x; v[1] += p0.y; v[2] += p0.z; v[3] += p0.w;
+            v[4] += p1.x; v[5] += p1.y; v[6] += p1.z; v[7] += p1.w;
         }
         if (f & SH_EPI_BIAS) {
             uint4 raw = __ldg(reinterpret_cast<const uint4 *>(a.bias + col));
@@ -108,22 +123,31 @@ __device__ __forceinline__ void epilogue8(const GemmArgs &a, uint32_t row, uint3
                 v[2 * i + 1] += t.y;
             }
         }
-        uint4 out;
-        __half2 *o = reinterpret_cast<__half2 *>(&out);
+        if (z32) {
+            reinterpret_cast<float4 *>(zf)[0] = make_float4(v[0], v[1], v[2], v[3]);
+            reinterpret_cast<float4 *>(zf)[1] = make_float4(v[4], v[5], v[6], v[7]);
+        } else {
+            uint4 out;
+            __half2 *o = reinterpret_cast<__half2 *>(&out);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) o[i] = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
-        *reinterpret_cast<uint4 *>(zp) = out;
+            for (int i = 0; i < 4; ++i) o[i] = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+            *reinterpret_cast<uint4 *>(zp) = out;
+        }
     } else {
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             const uint32_t c = col + i;
             if (c >= a.N) break;
             float t = v[i];
-            if (f & SH_EPI_ACCUMULATE) t += __half2float(zp[i]);
+            if (f & SH_EPI_ACCUMULATE) t += z32 ? zf[i] : __half2float(zp[i]);
+            if (f & SH_EPI_ACC_F32_IN) t += rf[i];
             if (f & SH_EPI_BIAS) t += __half2float(a.bias[c]);
             if (f & SH_EPI_GELU) t = gelu_fast(t);
             if (f & SH_EPI_RESIDUAL) t += __half2float(a.resid[(size_t)row * a.ldr + c]);
-            zp[i] = __float2half_rn(t);
+            if (z32)
+                zf[i] = t;
+            else
+                zp[i] = __float2half_rn(t);
         }
     }
 }
@@ -342,7 +366,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 float v[32];
 #pragma unroll
                 for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-                if (a.vec && row < a.M && col + 32 <= a.N) {
+                if (a.vec && row < a.M && col + 32 <= a.N && !(a.flags & (SH_EPI_F32_OUT | SH_EPI_ACC_F32_IN))) {
                     epilogue32(a, row, col, v, res);
                 } else {
 #pragma unroll
@@ -517,8 +541,9 @@ int gemm_run(uint64_t x, uint64_t w, uint64_t z, uint32_t M, uint32_t N, uint32_
              const char *name) {
     if (M == 0 || N == 0) return 0;
     if (!x || !w || !z || ldx < K || ldw < N || ldz < N || ((flags & SH_EPI_BIAS) && !bias) ||
-        ((flags & SH_EPI_RESIDUAL) && (!resid || ldr < N))) {
-        set_error(-1, "[%s] bad operands: %ux%ux%u ld %u/%u/%u", name, M, N, K, ldx, ldw, ldz);
+        ((flags & (SH_EPI_RESIDUAL | SH_EPI_ACC_F32_IN)) && (!resid || ldr < N)) ||
+        ((flags & SH_EPI_RESIDUAL) && (flags & SH_EPI_ACC_F32_IN))) {
+        set_error(-1, "[%s] bad operands: %ux%ux%u ld %u/%u/%u flags %#x", name, M, N, K, ldx, ldw, ldz, flags);
         return -1;
     }
     DeviceState &s = state();
@@ -533,10 +558,11 @@ int gemm_run(uint64_t x, uint64_t w, uint64_t z, uint32_t M, uint32_t N, uint32_
     a.K = K;
     a.ldz = ldz;
     a.ldr = ldr;
-    a.flags = flags & (SH_EPI_ACCUMULATE | SH_EPI_BIAS | SH_EPI_GELU | SH_EPI_RESIDUAL);
+    a.flags = flags & (SH_EPI_ACCUMULATE | SH_EPI_BIAS | SH_EPI_GELU | SH_EPI_RESIDUAL | SH_EPI_F32_OUT |
+                       SH_EPI_ACC_F32_IN);
     a.err = s.dev_err;
     a.vec = aligned16(z) && ldz % 8 == 0 && (!(flags & SH_EPI_BIAS) || aligned16(bias)) &&
-            (!(flags & SH_EPI_RESIDUAL) || (aligned16(resid) && ldr % 8 == 0));
+            (!(flags & (SH_EPI_RESIDUAL | SH_EPI_ACC_F32_IN)) || (aligned16(resid) && ldr % 8 == 0));
 
     const bool tc = !(flags & SH_GEMM_SIMT) && K > 0 && aligned16(x) && aligned16(w) && ldx % 8 == 0 &&
                     ldw % 8 == 0 && encode_tiled() != nullptr;

@@ -215,6 +215,13 @@ __host__ __device__ constexpr uint32_t umma_idesc_f16(uint32_t M, uint32_t N, ui
     return (1u << 4) | (a_mn_major << 15) | (b_mn_major << 16) | ((N >> 3) << 17) | ((M >> 4) << 24);
 }
 
+// 2^x with the hardware ex2.approx.ftz.f32 (relative error ~2^-22; 2^-inf = 0).
+__device__ __forceinline__ float fast_exp2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 // tanh-GELU 0.5 x (1 + tanh(u)), u = sqrt(2/pi) (x + 0.044715 x^3), with the hardware tanh.approx.f32 (relative
 // error about 2^-11, the precision of the fp16 result the epilogue stores).
 __device__ __forceinline__ float gelu_fast(float x) {

@@ -166,7 +166,7 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) k_softmax_vec(__half *y, 
         if (lane + 32 * i < cv) {
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
-                t[i].v[j] = exp2f(t[i].v[j] - m);
+                t[i].v[j] = fast_exp2(t[i].v[j] - m);
                 sum += t[i].v[j];
             }
         }
@@ -201,12 +201,128 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) k_softmax_any(__half *y, 
     for (uint32_t c = lane; c < cols; c += 32) yr[c] = __float2half_rn(exp2f(__half2float(xr[c]) * s2 - m) * inv);
 }
 
+// ---- wide rows (cols > 1024): one CTA of kRowThreads per row, the row in registers, block reductions ----------
+constexpr int kRowThreads = 128;
+
+template <int NT>
+__device__ __forceinline__ float block_sum(float v, float *red) {
+    v = warp_sum(v);
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    __syncthreads();
+    if (l == 0) red[w] = v;
+    __syncthreads();
+    float t = (l < NT / 32) ? red[l] : 0.f;
+    return warp_sum(t);
+}
+template <int NT>
+__device__ __forceinline__ float block_max(float v, float *red) {
+    v = warp_max(v);
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    __syncthreads();
+    if (l == 0) red[w] = v;
+    __syncthreads();
+    float t = (l < NT / 32) ? red[l] : -INFINITY;
+    return warp_max(t);
+}
+
+template <int VPT, bool ADD>
+__global__ void __launch_bounds__(kRowThreads) k_layernorm_row(__half *y, __half *h, const __half *a, const __half *b,
+                                                               const __half *g, const __half *be, uint32_t cols,
+                                                               uint32_t ld, float eps) {
+    __shared__ float red[kRowThreads / 32];
+    const size_t row = blockIdx.x;
+    const uint32_t cv = cols >> 3;
+    Vec8 x[VPT];
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+        const uint32_t v = threadIdx.x + kRowThreads * i;
+        if (v < cv) {
+            x[i] = load8(a + row * ld + 8 * v);
+            if (ADD) {
+                Vec8 bb = load8(b + row * ld + 8 * v);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) x[i].v[j] = __half2float(__float2half_rn(x[i].v[j] + bb.v[j]));
+                store8(h + row * ld + 8 * v, x[i]);
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) s += x[i].v[j];
+        }
+    }
+    const float mean = block_sum<kRowThreads>(s, red) / (float)cols;
+    float q = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i)
+        if (threadIdx.x + kRowThreads * i < cv) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const float d = x[i].v[j] - mean;
+                q += d * d;
+            }
+        }
+    const float rstd = rsqrtf(block_sum<kRowThreads>(q, red) / (float)cols + eps);
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+        const uint32_t v = threadIdx.x + kRowThreads * i;
+        if (v < cv) {
+            Vec8 gg = load8(g + 8 * v), bb = load8(be + 8 * v), o;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) o.v[j] = (x[i].v[j] - mean) * rstd * gg.v[j] + bb.v[j];
+            store8(y + row * ld + 8 * v, o);
+        }
+    }
+}
+
+template <int VPT, int NT = kRowThreads>
+__global__ void __launch_bounds__(NT) k_softmax_row(__half *y, const __half *x, uint32_t cols, uint32_t ld,
+                                                    float scale) {
+    __shared__ float red[kRowThreads / 32];
+    const size_t row = blockIdx.x;
+    const uint32_t cv = cols >> 3;
+    const float s2 = scale * 1.4426950408889634f;
+    Vec8 t[VPT];
+    float m = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+        const uint32_t v = threadIdx.x + NT * i;
+        if (v < cv) {
+            t[i] = load8(x + row * ld + 8 * v);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                t[i].v[j] *= s2;
+                m = fmaxf(m, t[i].v[j]);
+            }
+        }
+    }
+    m = block_max<NT>(m, red);
+    float sum = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i)
+        if (threadIdx.x + NT * i < cv) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                t[i].v[j] = fast_exp2(t[i].v[j] - m);
+                sum += t[i].v[j];
+            }
+        }
+    const float inv = 1.f / block_sum<NT>(sum, red);
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+        const uint32_t v = threadIdx.x + NT * i;
+        if (v < cv) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) t[i].v[j] *= inv;
+            store8(y + row * ld + 8 * v, t[i]);
+        }
+    }
+}
+
 // ---- elementwise ---------------------------------------------------------------------------------------------
 enum EwOp : int { kGelu = 0, kAdd = 1, kBias = 2, kScale = 3 };
 
 template <int OP>
 __device__ __forceinline__ float ew_apply(float x, float b, float s) {
-    if (OP == kGelu) return gelu_tanh(x);
+    if (OP == kGelu) return gelu_fast(x);
     if (OP == kAdd || OP == kBias) return x + b;
     return x * s;
 }
@@ -242,8 +358,39 @@ __global__ void k_ew_any(__half *y, const __half *x, const __half *b, uint32_t r
     }
 }
 
-// ---- transpose: 64 x 64 tiles through padded shared memory (bit-exact data movement) ------------------------
+// ---- transpose: 64 x 64 tiles through shared memory (bit-exact data movement) ------------------------------------
 constexpr int TT = 64;
+
+// Full aligned tiles: the tile is kept transposed in shared memory as 32-bit pairs, tT[c][p] = (x[2p][c], x[2p+1][c]),
+// 32 words per source column, the 16-byte groups of each row XOR-swizzled by (c % 8). Warp w loads 16-byte chunk w of
+// rows 2p, 2p+1 (p = lane) and writes 8 pair words (conflict-free: one row c per instruction, 32 consecutive p);
+// the store phase reads 16-byte groups (8 source rows) and writes them as one vector of an output row.
+__global__ void __launch_bounds__(256) k_transpose_pairs(__half *dst, const __half *src, uint32_t rows, uint32_t cols,
+                                                         uint32_t ld_src, uint32_t ld_dst) {
+    __shared__ __align__(16) uint32_t tT[TT * 32];
+    const uint32_t r0 = blockIdx.y * TT, c0 = blockIdx.x * TT;
+    const uint16_t *s16 = reinterpret_cast<const uint16_t *>(src);
+    uint16_t *d16 = reinterpret_cast<uint16_t *>(dst);
+    const uint32_t p = threadIdx.x & 31, q = threadIdx.x >> 5;   // row pair, 16-byte chunk (8 columns)
+    const uint4 a = *reinterpret_cast<const uint4 *>(s16 + (size_t)(r0 + 2 * p) * ld_src + c0 + 8 * q);
+    const uint4 b = *reinterpret_cast<const uint4 *>(s16 + (size_t)(r0 + 2 * p + 1) * ld_src + c0 + 8 * q);
+    const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, bw[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        const uint32_t c = 8 * q + k;
+        const uint32_t lo = (k & 1) ? (aw[k >> 1] >> 16) : (aw[k >> 1] & 0xFFFFu);
+        const uint32_t hi = (k & 1) ? (bw[k >> 1] >> 16) : (bw[k >> 1] & 0xFFFFu);
+        tT[c * 32 + (((p >> 2) ^ (c & 7)) << 2) + (p & 3)] = lo | (hi << 16);
+    }
+    __syncthreads();
+#pragma unroll
+    for (int it = 0; it < 2; ++it) {
+        const uint32_t idx = threadIdx.x + 256 * it;
+        const uint32_t c = idx >> 3, g = idx & 7;   // output row (source column), 16-byte group = 8 source rows
+        const uint4 v = *reinterpret_cast<const uint4 *>(&tT[c * 32 + ((g ^ (c & 7)) << 2)]);
+        *reinterpret_cast<uint4 *>(d16 + (size_t)(c0 + c) * ld_dst + r0 + 8 * g) = v;
+    }
+}
 __global__ void __launch_bounds__(256) k_transpose(__half *dst, const __half *src, uint32_t rows, uint32_t cols,
                                                    uint32_t ld_src, uint32_t ld_dst, int vec) {
     __shared__ uint16_t tile[TT][TT + 2];
@@ -334,7 +481,14 @@ void launch_layernorm(uint64_t y, uint64_t h, uint64_t a, uint64_t b, uint64_t g
     bool vec = cols % 8 == 0 && cols <= 32u * 8u * kMaxVecPerLane && vec_ok(y, ld) && vec_ok(a, ld) &&
                sh::aligned16(g) && sh::aligned16(be);
     if (ADD) vec = vec && vec_ok(h, ld) && vec_ok(b, ld);
-    if (vec) {
+    if (vec && cols > 1024) {
+        const uint32_t vpt = (cols / 8 + kRowThreads - 1) / kRowThreads;   // 2..4 vectors per thread
+#define SH_LNR(n) \
+    k_layernorm_row<n, ADD><<<rows, kRowThreads, 0, st>>>((__half *)y, (__half *)h, (const __half *)a, \
+                                                         (const __half *)b, (const __half *)g, (const __half *)be, cols, ld, eps)
+        if (vpt <= 2) SH_LNR(2); else if (vpt <= 3) SH_LNR(3); else SH_LNR(4);
+#undef SH_LNR
+    } else if (vec) {
         const int vpl = (int)((cols / 8 + 31) / 32);
         switch (vpl) {
 #define SH_LN_CASE(n) \
@@ -382,7 +536,12 @@ void sh_softmax_rows(uint64_t y, uint64_t x, uint32_t rows, uint32_t cols, uint3
     }
     cudaStream_t st = sh::stream();
     const bool vec = cols % 8 == 0 && cols <= 32u * 8u * kMaxVecPerLane && vec_ok(y, ld) && vec_ok(x, ld);
-    if (vec) {
+    if (vec && cols > 1024) {
+        const uint32_t vpt = (cols / 8 + kRowThreads - 1) / kRowThreads;
+#define SH_SMR(n) k_softmax_row<n><<<rows, kRowThreads, 0, st>>>((__half *)y, (const __half *)x, cols, ld, scale)
+        if (vpt <= 2) SH_SMR(2); else if (vpt <= 3) SH_SMR(3); else SH_SMR(4);
+#undef SH_SMR
+    } else if (vec) {
         switch ((int)((cols / 8 + 31) / 32)) {
 #define SH_SM_CASE(n) \
     case n: sm_vec_launch<n>(y, x, rows, cols, ld, scale, st); break;
@@ -420,8 +579,15 @@ void sh_transpose(uint64_t dst, uint64_t src, uint32_t rows, uint32_t cols, uint
         return;
     }
     const int vec = vec_ok(src, ld_src) && vec_ok(dst, ld_dst);
-    dim3 grid((cols + TT - 1) / TT, (rows + TT - 1) / TT);
-    k_transpose<<<grid, 256, 0, sh::stream()>>>((__half *)dst, (const __half *)src, rows, cols, ld_src, ld_dst, vec);
+    if (vec && rows % TT == 0 && cols % TT == 0) {
+        dim3 grid(cols / TT, rows / TT);
+        k_transpose_pairs<<<grid, 256, 0, sh::stream()>>>((__half *)dst, (const __half *)src, rows, cols, ld_src,
+                                                          ld_dst);
+    } else {
+        dim3 grid((cols + TT - 1) / TT, (rows + TT - 1) / TT);
+        k_transpose<<<grid, 256, 0, sh::stream()>>>((__half *)dst, (const __half *)src, rows, cols, ld_src, ld_dst,
+                                                    vec);
+    }
     sh::cuda_ok(cudaGetLastError(), "sh_transpose");
 }
 

@@ -320,6 +320,36 @@ int sh_cuda_device_error(void) {
 }
 
 int sh_cuda_num_sms(void) { return state().num_sms; }
+
+void *sh_cuda_ipc_alloc(size_t bytes) {
+    void *p = nullptr;
+    if (!cuda_ok(cudaMalloc(&p, bytes), "sh_cuda_ipc_alloc")) return nullptr;
+    cudaMemset(p, 0, bytes);
+    return p;
+}
+int sh_cuda_ipc_free(void *p) { return cuda_ok(cudaFree(p), "sh_cuda_ipc_free") ? 0 : -1; }
+int sh_cuda_ipc_handle(void *p, void *handle64) {
+    cudaIpcMemHandle_t h;
+    if (!cuda_ok(cudaIpcGetMemHandle(&h, p), "sh_cuda_ipc_handle")) return -1;
+    memcpy(handle64, &h, sizeof h < 64 ? sizeof h : 64);
+    return 0;
+}
+void *sh_cuda_ipc_open(const void *handle64) {
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle64, sizeof h < 64 ? sizeof h : 64);
+    void *p = nullptr;
+    if (!cuda_ok(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess), "sh_cuda_ipc_open")) return nullptr;
+    return p;
+}
+int sh_cuda_ipc_close(void *p) { return cuda_ok(cudaIpcCloseMemHandle(p), "sh_cuda_ipc_close") ? 0 : -1; }
+int sh_cuda_copy2d(uint64_t dst, size_t dpitch, uint64_t src, size_t spitch, size_t width_bytes, size_t rows,
+                   void *st) {
+    return cuda_ok(cudaMemcpy2DAsync((void *)dst, dpitch, (const void *)src, spitch, width_bytes, rows,
+                                     cudaMemcpyDefault, (cudaStream_t)st),
+                   "sh_cuda_copy2d")
+               ? 0
+               : -1;
+}
 float sh_cuda_timer_last_ms(void) { return g_last_timer_ms; }
 uint32_t sh_cuda_abi_version(void) { return 1; }
 

@@ -80,6 +80,24 @@ __global__ void k_fill_normal(__half *a, uint32_t rows, uint32_t cols, uint32_t 
     }
 }
 
+// sub-block [row0.., col0..] of a global gcols-wide LCG matrix: element (r, c) is draw (row0 + r) * gcols + col0 + c
+__global__ void k_fill_lcg_block(__half *a, uint32_t rows, uint32_t cols, uint32_t ld, uint32_t seed, int lo,
+                                 uint32_t span, float scale, uint64_t row0, uint64_t col0, uint64_t gcols) {
+    const uint32_t chunks = (cols + kChunk - 1) / kChunk;
+    const uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= (uint64_t)rows * chunks) return;
+    const uint32_t r = (uint32_t)(t / chunks), c0 = (uint32_t)(t - (uint64_t)r * chunks) * kChunk;
+    const uint64_t start = (row0 + r) * gcols + col0 + c0;
+    const Affine j = lcg_jump(start);
+    uint32_t s = j.a * (seed ^ kSeedXor) + j.c;
+    const uint32_t end = c0 + kChunk < cols ? c0 + kChunk : cols;
+    for (uint32_t c = c0; c < end; ++c) {
+        s = s * kA + kC;
+        const int v = lo + (int)((s >> 8) % span);
+        a[(size_t)r * ld + c] = __float2half_rn((float)v * scale);
+    }
+}
+
 __global__ void k_fill_parity(uint16_t *a, uint32_t rows, uint32_t cols, uint32_t ld, uint16_t even, uint16_t odd) {
     const uint64_t total = (uint64_t)rows * cols;
     for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < total; i += (uint64_t)gridDim.x * blockDim.x) {
@@ -130,6 +148,16 @@ void sh_cuda_fill_normal_fp16(uint64_t a, uint32_t rows, uint32_t cols, uint32_t
     const uint32_t grid = (uint32_t)((threads + 255) / 256);
     k_fill_normal<<<grid, 256, 0, sh::stream()>>>((__half *)a, rows, cols, ld, seed, mean, stdev);
     sh::cuda_ok(cudaGetLastError(), "sh_cuda_fill_normal_fp16");
+}
+
+void sh_cuda_fill_lcg_block(uint64_t a, uint32_t rows, uint32_t cols, uint32_t ld, uint32_t seed, int lo, int hi,
+                            float scale, uint64_t row0, uint64_t col0, uint64_t gcols) {
+    if (rows == 0 || cols == 0) return;
+    const uint64_t threads = (uint64_t)rows * ((cols + kChunk - 1) / kChunk);
+    const uint32_t grid = (uint32_t)((threads + 255) / 256);
+    k_fill_lcg_block<<<grid, 256, 0, sh::stream()>>>((__half *)a, rows, cols, ld, seed, lo, (uint32_t)(hi - lo + 1),
+                                                     scale, row0, col0, gcols);
+    sh::cuda_ok(cudaGetLastError(), "sh_cuda_fill_lcg_block");
 }
 
 void sh_test_fill_int_fp16(uint64_t a, uint32_t rows, uint32_t cols, uint32_t ld, uint32_t seed, int lo, int hi) {

@@ -77,10 +77,15 @@ SIGNATURES: dict[str, tuple] = {
     "sh_cuda_attention_batched": (i32, [u64, u64, u64, u64, u32, u32, u32, u32, u32, u32, u32, f32, u32]),
     "sh_cuda_fill_normal_fp16": (None, [u64, u32, u32, u32, u32, f32, f32]),
     "sh_cuda_gemm_splitk_noalloc": (i32, [u64, u64, u64, u32, u32, u32, u32, u32, u32, u64, u64, u32, u32, u32]),
+    "sh_cuda_fill_lcg_block": (None, [u64, u32, u32, u32, u32, i32, i32, f32, u64, u64, u64]),
+    "sh_cuda_ipc_alloc": (vp, [sz]), "sh_cuda_ipc_free": (i32, [vp]), "sh_cuda_ipc_handle": (i32, [vp, vp]),
+    "sh_cuda_ipc_open": (vp, [vp]), "sh_cuda_ipc_close": (i32, [vp]),
+    "sh_cuda_copy2d": (i32, [u64, sz, u64, sz, sz, sz, vp]),
 }
 
 # sh_ops_cuda.h constants
 EPI_ACCUMULATE, EPI_BIAS, EPI_GELU, EPI_RESIDUAL, GEMM_SIMT = 0x1, 0x2, 0x4, 0x8, 0x100
+EPI_F32_OUT, EPI_ACC_F32_IN = 0x10, 0x20
 SH_ALL = 0xFFFFFFFF
 SH_FP16, SH_FP8, SH_INT16, SH_INT8 = 0, 1, 2, 3
 SH_XM_AUTO, SH_XM_PANEL, SH_XM_WHOLE = 0, 1, 2

@@ -177,3 +177,25 @@ def test_xmcast_small_m(gpu_lib):
         assert lib.sh_gemm_xmcast_ex(dx, dw, dz, M, N, K, ldx, N, N, cfg, mode) == 0
         rt.check()
         _close(rt.get(dz, M, N), ops.gemm(x[:, :K], w), K)
+
+
+def test_fp32_carried_k_split(gpu_lib):
+    """SH_EPI_F32_OUT / SH_EPI_ACC_F32_IN: a K = 3 x 1024 product done as three calls with the running sum kept in
+    fp32 equals the one-call product to within one final fp16 rounding."""
+    rt, lib = gpu_lib, gpu_lib.lib
+    rt.reset()
+    M, N, Kp = 256, 384, 1024
+    xs = [lcg.uniform_fp16(M, Kp, 50 + i) for i in range(3)]
+    ws = [lcg.uniform_fp16(Kp, N, 60 + i) for i in range(3)]
+    dx = [rt.upload(x) for x in xs]
+    dw = [rt.upload(w) for w in ws]
+    acc = rt.alloc_bytes(M * N * 4)
+    z = rt.alloc(M, N)
+    assert lib.sh_cuda_gemm(dx[0], dw[0], acc, M, N, Kp, Kp, N, N, 0, 0, 0, L.EPI_F32_OUT, 0) == 0
+    assert lib.sh_cuda_gemm(dx[1], dw[1], acc, M, N, Kp, Kp, N, N, 0, 0, 0, L.EPI_F32_OUT | L.EPI_ACCUMULATE, 2) == 0
+    assert lib.sh_cuda_gemm(dx[2], dw[2], z, M, N, Kp, Kp, N, N, 0, acc, N, L.EPI_ACC_F32_IN, 0) == 0
+    rt.check()
+    want = sum(ops.gemm(x, w) for x, w in zip(xs, ws))
+    _close(rt.get(z, M, N), want, 3 * Kp)
+    err = np.abs(rt.get(z, M, N).astype(np.float32) - want)
+    assert float(err.max()) <= 2.0 ** -10 * float(np.abs(want).max()) + 1e-3

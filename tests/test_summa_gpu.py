@@ -1,0 +1,65 @@
+"""SUMMA on the GPU: bit-exact block generation, the panel pipeline on one GPU, and the multi-GPU run (2+ GPUs,
+as torch.distributed ranks over NCCL with IPC panel pulls)."""
+from __future__ import annotations
+
+import os
+import subprocess
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import lcg
+from softhier_cuda import summa as SU
+
+pytestmark = pytest.mark.gpu
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def test_lcg_block_fill_is_a_slice_of_the_global_fill(gpu_lib):
+    rt, lib = gpu_lib, gpu_lib.lib
+    rt.reset()
+    R, C = 300, 500
+    full = lcg.fill_fp16(R, C, 77, -1024, 1023, 1 / 1024)
+    for r0, c0, rows, cols in [(0, 0, 300, 500), (17, 33, 100, 200), (299, 499, 1, 1), (64, 256, 128, 244)]:
+        a = rt.alloc(rows, cols + 3)
+        lib.sh_cuda_fill_lcg_block(a, rows, cols, cols + 3, 77, -1024, 1023, 1 / 1024, r0, c0, C)
+        rt.check()
+        got = rt.get(a, rows, cols, cols + 3)
+        assert (got.view(np.uint16) == full[r0:r0 + rows, c0:c0 + cols].view(np.uint16)).all()
+
+
+@pytest.mark.parametrize("kb", [2048, 512])
+def test_summa_single_gpu_panels(gpu_lib, kb):
+    rt, lib = gpu_lib, gpu_lib.lib
+    n = 2048
+    lay = SU.Layout(n, n, n, 1, 1, kb)
+    su = SU.SummaGPU(lib, lay, 0, lambda x: [x], lambda: None, (torch.cuda.Stream(), torch.cuda.Stream()))
+    try:
+        su.fill_inputs(5, 6)
+        for _ in range(2):
+            assert su.step(torch) == 0
+        torch.cuda.synchronize()
+        rt.check()
+        c = torch.empty((n, n), dtype=torch.float16, device="cuda")
+        lib.sh_cuda_copy2d(c.data_ptr(), n * 2, su.c, n * 2, n * 2, n, None)
+        torch.cuda.synchronize()
+        want = lcg.uniform_fp16(n, n, 5).astype(np.float32) @ lcg.uniform_fp16(n, n, 6).astype(np.float32)
+        err = np.abs(c.cpu().numpy().astype(np.float32) - want)
+        assert np.all(err <= 2e-2 + 2.0 ** -10 * np.abs(want)), float(err.max())
+    finally:
+        su.close()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_summa_multi_gpu():
+    world = 8 if torch.cuda.device_count() >= 8 else (4 if torch.cuda.device_count() >= 4 else 2)
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           f"--nproc-per-node={world}", "--master-addr=127.0.0.1", "--master-port=29533",
+           str(ROOT / "tests" / "summa_worker.py")]
+    r = subprocess.run(cmd, capture_output=True, text=True, env=env, timeout=360)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    assert r.stdout.count("SUMMA_OK") == world, r.stdout
