@@ -16,6 +16,7 @@
 // Every mbarrier wait is bounded (SH_SPIN_CYCLES): on a timeout the CTA raises the device error word, skips its
 // remaining work, waits for its outstanding TMA loads and frees its tensor memory.
 // Shapes the TMA path cannot address (16-byte alignment of base or leading dimension) use a CUDA-core kernel.
+#include <stdlib.h>
 #include <string.h>
 
 #include <mutex>
@@ -29,6 +30,8 @@ constexpr int BK = 64;
 constexpr int kThreads = 320;   // warp 0 TMA, warp 1 MMA, warps 2..9 epilogue
 constexpr uint32_t kEpiWarps = 8;
 
+constexpr uint32_t kEpiStageBytes = 8 * 4096;   // per epilogue warp: two 32 x 32 fp16 store tiles
+
 template <int BN>
 struct TileCfg {
     static constexpr int kStages = BN == 256 ? 4 : (BN == 128 ? 6 : 8);
@@ -36,7 +39,7 @@ struct TileCfg {
     static constexpr uint32_t kBBytes = BK * BN * 2;
     static constexpr uint32_t kStageBytes = kABytes + kBBytes;
     static constexpr uint32_t kTmemCols = 2 * BN;
-    static constexpr uint32_t kSmem = kStages * kStageBytes + 1024 + 256;
+    static constexpr uint32_t kSmem = kStages * kStageBytes + kEpiStageBytes + 1024 + 256;
 };
 
 struct GemmArgs {
@@ -45,7 +48,8 @@ struct GemmArgs {
     const __half *resid;
     uint32_t M, N, K, ldz, ldr, flags;
     uint32_t tiles_n, num_tiles, k_blocks, splits, kb_per_split;
-    uint32_t vec;   // epilogue may use 16-byte accesses on z / bias / resid
+    uint32_t vec;        // epilogue may use 16-byte accesses on z / bias / resid
+    uint32_t tma_store;  // fp16 Z written by TMA stores of 32 x 32 tiles staged in shared memory
     float *ws;
     uint32_t *counters;
     int *err;
@@ -165,14 +169,13 @@ __device__ __forceinline__ void add8(float *v, const uint4 &raw) {
         v[2 * i + 1] += t.y;
     }
 }
-// fused epilogue of 32 consecutive in-range columns of one row on the 16-byte path; `res` holds the residual
-__device__ __forceinline__ void epilogue32(const GemmArgs &a, uint32_t row, uint32_t col, float (&v)[32],
+// fused math of 32 consecutive in-range columns of one row on the 16-byte path; `res` holds the residual
+__device__ __forceinline__ void epi_math32(const GemmArgs &a, uint32_t row, uint32_t col, float (&v)[32],
                                            const uint4 (&res)[4]) {
     const uint32_t f = a.flags;
-    __half *zp = a.z + (size_t)row * a.ldz + col;
     if (f & SH_EPI_ACCUMULATE) {
         uint4 old[4];
-        load32(zp, old);
+        load32(a.z + (size_t)row * a.ldz + col, old);
 #pragma unroll
         for (int q = 0; q < 4; ++q) add8(v + 8 * q, old[q]);
     }
@@ -188,25 +191,88 @@ __device__ __forceinline__ void epilogue32(const GemmArgs &a, uint32_t row, uint
 #pragma unroll
         for (int q = 0; q < 4; ++q) add8(v + 8 * q, res[q]);
     }
+}
+
+// fused math of 32 columns of one row whose loads may leave the matrix (guarded, element by element)
+__device__ __forceinline__ void epi_math_guarded(const GemmArgs &a, uint32_t row, uint32_t col, float (&v)[32]) {
+    if (row >= a.M) return;
+    const uint32_t f = a.flags;
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-        uint4 out;
-        __half2 *o = reinterpret_cast<__half2 *>(&out);
+    for (int i = 0; i < 32; ++i) {   // fully unrolled: v stays in registers
+        const uint32_t c = col + i;
+        if (c >= a.N) continue;
+        float t = v[i];
+        if (f & SH_EPI_ACCUMULATE) t += __half2float(a.z[(size_t)row * a.ldz + c]);
+        if (f & SH_EPI_BIAS) t += __half2float(a.bias[c]);
+        if (f & SH_EPI_GELU) t = gelu_fast(t);
+        if (f & SH_EPI_RESIDUAL) t += __half2float(a.resid[(size_t)row * a.ldr + c]);
+        v[i] = t;
+    }
+}
+
+// One 32-column chunk of the tile per warp (thread = row): the fused epilogue, then either the warp's 32 x 32 tile
+// is staged in its shared-memory buffer (64-byte swizzle: 16-byte unit u of row r at u ^ ((r >> 1) & 3)) and written
+// by one TMA store, or every thread stores its row directly (fp32 outputs, unaligned operands).
+__device__ __forceinline__ void epi_chunk(const GemmArgs &a, const CUtensorMap *mz, uint8_t *stg, uint32_t &nst,
+                                          uint32_t row, uint32_t row_base, uint32_t col, float (&v)[32],
+                                          const uint4 (&res)[4], uint32_t lane) {
+    const bool inb = a.vec && row < a.M && col + 32 <= a.N;
+    if (a.tma_store) {
+        if (inb)
+            epi_math32(a, row, col, v, res);
+        else
+            epi_math_guarded(a, row, col, v);
+        uint8_t *buf = stg + (nst & 1u) * 2048;
+        if (lane == 0) bulk_wait_read1();     // the store issued from this buffer two chunks ago has read it
+        __syncwarp();
 #pragma unroll
-        for (int i = 0; i < 4; ++i) o[i] = __floats2half2_rn(v[8 * q + 2 * i], v[8 * q + 2 * i + 1]);
-        *reinterpret_cast<uint4 *>(zp + 8 * q) = out;
+        for (int q = 0; q < 4; ++q) {
+            uint4 out;
+            __half2 *o = reinterpret_cast<__half2 *>(&out);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) o[i] = __floats2half2_rn(v[8 * q + 2 * i], v[8 * q + 2 * i + 1]);
+            *reinterpret_cast<uint4 *>(buf + lane * 64 + ((q ^ ((lane >> 1) & 3u)) << 4)) = out;
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+            tma_store_2d(mz, buf, (int32_t)col, (int32_t)row_base);
+            bulk_commit();
+        }
+        ++nst;
+    } else if (inb && !(a.flags & (SH_EPI_F32_OUT | SH_EPI_ACC_F32_IN))) {
+        epi_math32(a, row, col, v, res);
+        __half *zp = a.z + (size_t)row * a.ldz + col;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            uint4 out;
+            __half2 *o = reinterpret_cast<__half2 *>(&out);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) o[i] = __floats2half2_rn(v[8 * q + 2 * i], v[8 * q + 2 * i + 1]);
+            *reinterpret_cast<uint4 *>(zp + 8 * q) = out;
+        }
+    } else {
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+            float w8[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) w8[i] = v[8 * g + i];
+            epilogue8(a, row, col + g * 8, w8);
+        }
     }
 }
 
 template <int BN>
 __global__ void __launch_bounds__(kThreads, 1)
-    k_gemm_tc(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w, GemmArgs a) {
+    k_gemm_tc(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w,
+              const __grid_constant__ CUtensorMap map_z, GemmArgs a) {
     using C = TileCfg<BN>;
     constexpr int S = C::kStages;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
     uint8_t *smem = smem_raw + pad;
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem + S * C::kStageBytes);
+    uint8_t *epi_stage = smem + S * C::kStageBytes;
+    uint64_t *full = reinterpret_cast<uint64_t *>(epi_stage + kEpiStageBytes);
     uint64_t *empty = full + S;
     uint64_t *tfull = empty + S;    // [2] accumulator ready for the epilogue
     uint64_t *tempty = tfull + 2;   // [2] accumulator drained by the epilogue
@@ -330,11 +396,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         constexpr uint32_t HB = BN / 2;            // columns per warp
         const uint32_t row_in_tile = quarter * 32 + lane;
         const bool want_res = (a.flags & SH_EPI_RESIDUAL) != 0;
+        uint8_t *stg = epi_stage + (warp - 2u) * 4096u;
+        uint32_t nst = 0;    // TMA stores this warp has issued
+        if (a.tma_store && lane == 0) prefetch_tmap(&map_z);
         uint32_t acc = 0, acc_phase = 0, es_phase = 0;
         for (uint32_t u = blockIdx.x; u < total_units; u += gridDim.x) {
             const uint32_t tile = u / a.splits, split = u - tile * a.splits;
             const uint32_t tm = tile / a.tiles_n, tn = tile - tm * a.tiles_n;
             const uint32_t row = tm * BM + row_in_tile;
+            const uint32_t row_base = tm * BM + quarter * 32;
             const uint32_t col0 = tn * BN + half * HB;
             // residual of the first chunk is fetched before the accumulator is ready
             uint4 res[4] = {};
@@ -366,17 +436,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 float v[32];
 #pragma unroll
                 for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-                if (a.vec && row < a.M && col + 32 <= a.N && !(a.flags & (SH_EPI_F32_OUT | SH_EPI_ACC_F32_IN))) {
-                    epilogue32(a, row, col, v, res);
-                } else {
-#pragma unroll
-                    for (int g = 0; g < 4; ++g) {
-                        float w8[8];
-#pragma unroll
-                        for (int i = 0; i < 8; ++i) w8[i] = v[8 * g + i];
-                        epilogue8(a, row, col + g * 8, w8);
-                    }
-                }
+                if (!a.tma_store || (row_base < a.M && col < a.N))
+                    epi_chunk(a, &map_z, stg, nst, row, row_base, col, v, res, lane);
 #pragma unroll
                 for (int i = 0; i < 4; ++i) res[i] = nres[i];
             }
@@ -417,6 +478,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (!epi_sync(esync, es_phase, abort, a.err)) break;
             }
         }
+        if (lane == 0 && nst) bulk_wait_all();   // the staging buffers stay live until every store completed
     }
 
     __syncwarp();
@@ -425,6 +487,196 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem_base, C::kTmemCols);
+    }
+}
+
+// ---- 2-CTA (cta_group::2) variant: a cluster of two CTAs on two SMs computes a 256 x BN tile -------------------
+// Each CTA loads its own 128 rows of the X tile and its own BN/2 columns of the W tile per stage (32 KB: 6 stages),
+// both CTAs' TMA transactions complete on the leader's `full` barrier, the leader's single thread issues
+// tcgen05.mma.cta_group::2 (M = 256), and its commits arrive on the `empty` / `tfull` barriers of both CTAs. Each
+// CTA's tensor memory holds its own 128 rows of the accumulator (all BN columns), which its 8 epilogue warps drain
+// exactly like the single-CTA kernel before arriving on the leader's `tempty` barrier (16 arrivals). Per stage and
+// SM, W traffic is half that of the single-CTA tile. No split-K (the caller picks this kernel only without it).
+constexpr int kPairStages = 6;
+
+template <int BN>
+struct PairCfg {
+    static constexpr uint32_t kABytes = 128 * BK * 2;          // this CTA's 128 rows
+    static constexpr uint32_t kBBytes = (BN / 2) * BK * 2;     // this CTA's BN/2 columns
+    static constexpr uint32_t kStageBytes = kABytes + kBBytes;
+    static constexpr uint32_t kTmemCols = 2 * BN;
+    static constexpr uint32_t kSmem = kPairStages * kStageBytes + kEpiStageBytes + 1024 + 256;
+};
+
+template <int BN>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    k_gemm_tc2(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w,
+               const __grid_constant__ CUtensorMap map_z, GemmArgs a) {
+    using C = PairCfg<BN>;
+    constexpr int S = kPairStages;
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
+    uint8_t *smem = smem_raw + pad;
+    uint8_t *epi_stage = smem + S * C::kStageBytes;
+    uint64_t *full = reinterpret_cast<uint64_t *>(epi_stage + kEpiStageBytes);
+    uint64_t *empty = full + S;
+    uint64_t *tfull = empty + S;
+    uint64_t *tempty = tfull + 2;
+    uint64_t *mdone = tempty + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mdone + 1);
+    volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const bool leader = rank == 0;
+    const uint32_t pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);     // leader: its producer's arrive.expect_tx of both CTAs' bytes
+            mbar_init(&empty[s], 1);    // both: the leader's commit
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&tfull[i], 1);                 // both: the leader's commit
+            mbar_init(&tempty[i], 2 * kEpiWarps);    // leader: every epilogue warp of both CTAs
+        }
+        mbar_init(mdone, 1);
+        *abort = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(tmem_slot, C::kTmemCols);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    cluster_sync_all();     // both CTAs' barriers exist before any peer signal reaches them
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    const uint32_t total_units = a.num_tiles;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            prefetch_tmap(&map_x);
+            prefetch_tmap(&map_w);
+            uint32_t stage = 0, phase = 0;
+            uint32_t armed[S];
+            for (int s = 0; s < S; ++s) armed[s] = 2;
+            bool ok = true;
+            for (uint32_t u = pair; ok && u < total_units; u += npairs) {
+                const uint32_t tm = u / a.tiles_n, tn = u - tm * a.tiles_n;
+                for (uint32_t kb = 0; kb < a.k_blocks; ++kb) {
+                    if (!mbar_wait(&empty[stage], phase ^ 1u, abort, a.err)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t *sa = smem + stage * C::kStageBytes;
+                    uint8_t *sb = sa + C::kABytes;
+                    const uint32_t bar = mapa_shared(smem_u32(&full[stage]), 0);
+                    if (leader) mbar_arrive_expect_tx(&full[stage], 2 * C::kStageBytes);
+                    armed[stage] = phase;
+                    tma_load_2d_pair(sa, &map_x, bar, (int32_t)(kb * BK), (int32_t)(tm * 256 + rank * 128));
+#pragma unroll
+                    for (int c = 0; c < BN / 128; ++c)
+                        tma_load_2d_pair(sb + c * (BK * 128), &map_w, bar,
+                                         (int32_t)(tn * BN + rank * (BN / 2) + c * 64), (int32_t)(kb * BK));
+                    if (++stage == S) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            // drain: a stage is free again only after the leader's MMAs read it, which is after its bytes landed
+            for (int s = 0; s < S; ++s)
+                if (armed[s] != 2) drain_wait(&empty[s], armed[s]);
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && leader) {
+            constexpr uint32_t idesc = umma_idesc_f16(256, BN, 0, 1);
+            uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
+            bool ok = true;
+            for (uint32_t u = pair; ok && u < total_units; u += npairs) {
+                if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort, a.err)) break;
+                tc_fence_after();
+                const uint32_t d = tmem_base + acc * BN;
+                for (uint32_t kb = 0; kb < a.k_blocks; ++kb) {
+                    if (!mbar_wait(&full[stage], phase, abort, a.err)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t sa = smem_u32(smem + stage * C::kStageBytes);
+                    const uint32_t sb = sa + C::kABytes;
+#pragma unroll
+                    for (int j = 0; j < BK / 16; ++j)
+                        umma_f16_ss_pair(d, sw128_desc(sa + j * 32, 16, 1024), sw128_desc(sb + j * 2048, BK * 128, 1024),
+                                         idesc, (kb > 0 || j > 0) ? 1u : 0u);
+                    umma_commit_pair_both(&empty[stage]);
+                    if (++stage == S) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                umma_commit_pair_both(&tfull[acc]);
+                acc ^= 1u;
+                if (acc == 0) acc_phase ^= 1u;
+            }
+            umma_commit_pair_both(mdone);   // both CTAs: every MMA the leader issued has completed
+        }
+        if (lane == 0) drain_wait(mdone, 0);
+    } else {
+        const uint32_t quarter = warp & 3u;
+        const uint32_t half = (warp - 2u) >> 2;
+        constexpr uint32_t HB = BN / 2;
+        const uint32_t row_in_tile = rank * 128 + quarter * 32 + lane;
+        const bool want_res = (a.flags & SH_EPI_RESIDUAL) != 0;
+        const uint32_t tempty_leader[2] = {mapa_shared(smem_u32(&tempty[0]), 0), mapa_shared(smem_u32(&tempty[1]), 0)};
+        uint8_t *stg = epi_stage + (warp - 2u) * 4096u;
+        uint32_t nst = 0;
+        if (a.tma_store && lane == 0) prefetch_tmap(&map_z);
+        uint32_t acc = 0, acc_phase = 0;
+        for (uint32_t u = pair; u < total_units; u += npairs) {
+            const uint32_t tm = u / a.tiles_n, tn = u - tm * a.tiles_n;
+            const uint32_t row = tm * 256 + row_in_tile;
+            const uint32_t row_base = tm * 256 + rank * 128 + quarter * 32;
+            const uint32_t col0 = tn * BN + half * HB;
+            uint4 res[4] = {};
+            const bool res_vec = want_res && a.vec && row < a.M;
+            if (res_vec && col0 + 32 <= a.N) load32(a.resid + (size_t)row * a.ldr + col0, res);
+            if (!mbar_wait(&tfull[acc], acc_phase, abort, a.err)) break;
+            tc_fence_after();
+            const uint32_t taddr = tmem_base + ((quarter * 32u) << 16) + acc * BN + half * HB;
+#pragma unroll 1
+            for (uint32_t c = 0; c < HB / 32; ++c) {
+                uint32_t r[32];
+                tmem_ld_32x32b_x32(taddr + c * 32, r);
+                tmem_ld_wait();
+                const uint32_t col = col0 + c * 32;
+                uint4 nres[4] = {};
+                if (res_vec && c + 1 < HB / 32 && col + 64 <= a.N)
+                    load32(a.resid + (size_t)row * a.ldr + col + 32, nres);
+                float v[32];
+#pragma unroll
+                for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+                if (!a.tma_store || (row_base < a.M && col < a.N))
+                    epi_chunk(a, &map_z, stg, nst, row, row_base, col, v, res, lane);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) res[i] = nres[i];
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(tempty_leader[acc]);
+            acc ^= 1u;
+            if (acc == 0) acc_phase ^= 1u;
+        }
+        if (lane == 0 && nst) bulk_wait_all();
+    }
+
+    __syncwarp();
+    tc_fence_before();
+    cluster_sync_all();     // neither CTA frees tensor memory while the pair may still use it
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem_base, C::kTmemCols);
     }
 }
 
@@ -489,6 +741,7 @@ bool set_smem_attr() {
 }
 
 struct Plan {
+    bool pair = false;            // 2-CTA kernel, 256 x 256 tiles
     int bn = 0;                   // 0: CUDA-core fallback
     uint32_t tiles_m = 0, tiles_n = 0, k_blocks = 0, splits = 1, kb_per_split = 0;
 };
@@ -515,16 +768,44 @@ Plan make_plan(uint32_t M, uint32_t N, uint32_t K, uint32_t splits_req, int num_
     }
     p.kb_per_split = (p.k_blocks + s - 1) / s;
     p.splits = (p.k_blocks + p.kb_per_split - 1) / p.kb_per_split;
+    // enough 256 x 256 tiles to keep every SM pair busy: the 2-CTA kernel (half the W traffic per SM)
+    static const int pair_env = [] {
+        const char *e = getenv("SH_GEMM_PAIR");
+        return e ? atoi(e) : -1;
+    }();
+    if (p.splits == 1 && p.bn == 256 && pair_env != 0 &&
+        (uint64_t)((M + 255) / 256) * p.tiles_n * 2 >= (uint64_t)num_sms)
+        p.pair = true;
     return p;
 }
 
 template <int BN>
-int launch_tc(const Plan &p, const CUtensorMap &mx, const CUtensorMap &mw, GemmArgs a, cudaStream_t st) {
+int launch_tc(const Plan &p, const CUtensorMap &mx, const CUtensorMap &mw, const CUtensorMap &mz, GemmArgs a,
+              cudaStream_t st) {
     if (!set_smem_attr<BN>()) return -1;
     const uint32_t units = p.tiles_m * p.tiles_n * p.splits;
     const uint32_t grid = min(units, (uint32_t)sh::state().num_sms);
-    k_gemm_tc<BN><<<grid, kThreads, TileCfg<BN>::kSmem, st>>>(mx, mw, a);
+    k_gemm_tc<BN><<<grid, kThreads, TileCfg<BN>::kSmem, st>>>(mx, mw, mz, a);
     return sh::cuda_ok(cudaGetLastError(), "sh_gemm launch") ? 0 : -1;
+}
+
+template <int BN>
+int launch_pair(const Plan &p, const CUtensorMap &mx, const CUtensorMap &mw, const CUtensorMap &mz, GemmArgs a,
+                cudaStream_t st) {
+    static bool done[sh::kMaxDevices] = {};
+    const int d = sh::current_device() % sh::kMaxDevices;
+    if (!done[d]) {
+        if (!sh::cuda_ok(cudaFuncSetAttribute(k_gemm_tc2<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              (int)PairCfg<BN>::kSmem),
+                         "cudaFuncSetAttribute(gemm pair)"))
+            return -1;
+        done[d] = true;
+    }
+    a.num_tiles = ((a.M + 255) / 256) * p.tiles_n;
+    a.splits = 1;
+    const uint32_t pairs = min(a.num_tiles, (uint32_t)sh::state().num_sms / 2);
+    k_gemm_tc2<BN><<<2 * pairs, kThreads, PairCfg<BN>::kSmem, st>>>(mx, mw, mz, a);
+    return sh::cuda_ok(cudaGetLastError(), "sh_gemm launch (pair)") ? 0 : -1;
 }
 
 uint32_t smem_of(int bn) {
@@ -586,16 +867,25 @@ int gemm_run(uint64_t x, uint64_t w, uint64_t z, uint32_t M, uint32_t N, uint32_
         a.counters = tile_counters(a.num_tiles);
         if (!a.ws || !a.counters) return -1;
     }
-    CUtensorMap mx, mw;
+    CUtensorMap mx, mw, mz;
     if (!make_map_2d(&mx, (const void *)x, M, K, ldx, BM, BK, true) ||
         !make_map_2d(&mw, (const void *)w, K, N, ldw, BK, 64, true)) {
         set_error(-1, "[%s] cuTensorMapEncodeTiled failed for %ux%ux%u", name, M, N, K);
         return -1;
     }
+    // fp16 results of single-pass tiles leave through TMA stores of 32 x 32 tiles (64-byte swizzled staging)
+    static const bool tma_store_env = [] {   // SH_GEMM_TMA_STORE=0: every thread stores its own row instead
+        const char *e = getenv("SH_GEMM_TMA_STORE");
+        return !(e && atoi(e) == 0);
+    }();
+    a.tma_store = tma_store_env && a.vec && p.splits == 1 && !(a.flags & (SH_EPI_F32_OUT | SH_EPI_ACC_F32_IN)) &&
+                  make_map_2d_sw(&mz, (const void *)z, M, N, ldz, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B);
+    if (!a.tma_store) mz = mx;   // not read by the kernel
+    if (p.pair) return launch_pair<256>(p, mx, mw, mz, a, st);
     switch (p.bn) {
-        case 256: return launch_tc<256>(p, mx, mw, a, st);
-        case 128: return launch_tc<128>(p, mx, mw, a, st);
-        default: return launch_tc<64>(p, mx, mw, a, st);
+        case 256: return launch_tc<256>(p, mx, mw, mz, a, st);
+        case 128: return launch_tc<128>(p, mx, mw, mz, a, st);
+        default: return launch_tc<64>(p, mx, mw, mz, a, st);
     }
 }
 
@@ -817,15 +1107,15 @@ extern "C" int sh_cuda_gemm_splitk_noalloc(uint64_t x, uint64_t w, uint64_t z, u
     switch (p.bn) {
         case 256:
             if (!set_smem_attr<256>()) return -1;
-            k_gemm_tc<256><<<grid, kThreads, TileCfg<256>::kSmem, st>>>(mx, mw, a);
+            k_gemm_tc<256><<<grid, kThreads, TileCfg<256>::kSmem, st>>>(mx, mw, mx, a);
             break;
         case 128:
             if (!set_smem_attr<128>()) return -1;
-            k_gemm_tc<128><<<grid, kThreads, TileCfg<128>::kSmem, st>>>(mx, mw, a);
+            k_gemm_tc<128><<<grid, kThreads, TileCfg<128>::kSmem, st>>>(mx, mw, mx, a);
             break;
         default:
             if (!set_smem_attr<64>()) return -1;
-            k_gemm_tc<64><<<grid, kThreads, TileCfg<64>::kSmem, st>>>(mx, mw, a);
+            k_gemm_tc<64><<<grid, kThreads, TileCfg<64>::kSmem, st>>>(mx, mw, mx, a);
             break;
     }
     return sh::cuda_ok(cudaGetLastError(), name) ? 0 : -1;

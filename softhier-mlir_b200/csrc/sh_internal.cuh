@@ -65,6 +65,9 @@ PFN_encodeTiled encode_tiled();
 // 2-D fp16 row-major tensor [rows, cols] (leading dim ld elements), box [box_rows, box_cols], 128-B swizzle.
 bool make_map_2d(CUtensorMap *m, const void *base, uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_rows,
                  uint32_t box_cols, bool swizzle128);
+// the same with an explicit swizzle mode (64-byte swizzle for the 32 x 32 epilogue store tiles)
+bool make_map_2d_sw(CUtensorMap *m, const void *base, uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_rows,
+                    uint32_t box_cols, CUtensorMapSwizzle sw);
 // 3-D fp16 tensor [batches, rows, cols]: row stride ld elements, batch stride batch_ld elements, box
 // [1, box_rows, box_cols], 128-byte swizzle. Rows past `rows` inside a batch read as zeros.
 bool make_map_3d(CUtensorMap *m, const void *base, uint64_t batches, uint64_t rows, uint64_t cols, uint64_t ld,
@@ -148,6 +151,17 @@ __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *m, uin
         "l"(reinterpret_cast<uint64_t>(m)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
         : "memory");
 }
+// 2-D TMA store of a shared-memory tile to global memory (out-of-bounds elements are not written).
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap *m, const void *src, int32_t x, int32_t y) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                     reinterpret_cast<uint64_t>(m)),
+                 "r"(smem_u32(src)), "r"(x), "r"(y)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 // Make this thread's generic-proxy shared-memory writes visible to the async proxy (TMA / tensor cores).
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -209,6 +223,66 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr, uint32_t lbo, uin
     d |= (uint64_t)2 << 61;   // SWIZZLE_128B
     return d;
 }
+// ---- clusters of two CTAs (tcgen05 cta_group::2) ------------------------------------------------------
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {   // every thread of both CTAs
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// shared::cluster address of the same shared variable in CTA `rank` of the cluster
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+// 2-D TMA load into this CTA's shared memory whose completion is counted on the barrier at `bar_cluster_addr`
+// (the pair leader's barrier); no cluster broadcast.
+__device__ __forceinline__ void tma_load_2d_pair(void *dst, const CUtensorMap *m, uint32_t bar_cluster_addr, int32_t x,
+                                                 int32_t y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, "
+        "%4}], [%2];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(m)), "r"(bar_cluster_addr), "r"(x), "r"(y)
+        : "memory");
+}
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t *slot, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)),
+                 "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+// D (both CTAs' tensor memory) (+)= A (M/2 rows in each CTA) . B (N/2 columns in each CTA); leader CTA only
+__device__ __forceinline__ void umma_f16_ss_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                                 uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// Arrive once on the barrier at the same offset in both CTAs of the pair when the leader's MMAs are complete: one
+// commit per CTA, each to that CTA's barrier through its shared::cluster address.
+__device__ __forceinline__ void umma_commit_pair_both(uint64_t *bar) {
+    const uint32_t local = smem_u32(bar);
+#pragma unroll
+    for (uint32_t r = 0; r < 2; ++r)
+        asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                         mapa_shared(local, r))
+                     : "memory");
+}
+
 // Instruction descriptor: fp16 A/B, fp32 D, M x N tile, A and B majorness (0 = K-major, 1 = MN-major).
 __host__ __device__ constexpr uint32_t umma_idesc_f16(uint32_t M, uint32_t N, uint32_t a_mn_major,
                                                       uint32_t b_mn_major) {

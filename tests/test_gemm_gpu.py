@@ -199,3 +199,12 @@ def test_fp32_carried_k_split(gpu_lib):
     _close(rt.get(z, M, N), want, 3 * Kp)
     err = np.abs(rt.get(z, M, N).astype(np.float32) - want)
     assert float(err.max()) <= 2.0 ** -10 * float(np.abs(want).max()) + 1e-3
+
+
+@pytest.mark.parametrize("M,N,K,flags", [(8192, 768, 768, 0), (8192, 2304, 768, L.EPI_BIAS),
+                                         (8000, 768, 3072, L.EPI_BIAS | L.EPI_RESIDUAL),
+                                         (8192, 3072, 768, L.EPI_BIAS | L.EPI_GELU), (9984, 1024, 640, 0)])
+def test_pair_tiles(gpu_lib, M, N, K, flags):
+    """Shapes with enough 256 x 256 tiles run on the 2-CTA (cta_group::2) kernel."""
+    got, want = _run(gpu_lib, M, N, K, flags=flags)
+    _close(got, want, K)
