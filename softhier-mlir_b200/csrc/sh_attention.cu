@@ -3,12 +3,14 @@
 //
 // The reference keeps a whole sq x S score block in one cluster's TCDM (no online softmax), so S is bounded by
 // L1. Here attention is flash-style with an online softmax, so S is unbounded:
-//   - k_attn_tc (sm_100a tensor cores, dh = 64): one CTA per (sequence, head, 128 query rows); Q/K/V tiles come
-//     in by TMA, S = Q K^T accumulates in tensor memory (tcgen05.mma), the softmax runs in registers from
-//     tcgen05.ld, P (fp16) goes to shared memory and O += P V accumulates in tensor memory;
+//   - k_attn_tc (sm_100a tensor cores, dh = 64): persistent, one CTA per SM over (sequence, head, 256 query rows)
+//     items; Q/K/V tiles come in by TMA, S = Q K^T accumulates in tensor memory (tcgen05.mma), the softmax runs in
+//     registers from tcgen05.ld, P (fp16) goes to shared memory and O += P V accumulates in tensor memory;
 //   - k_attn_simt: CUDA-core fallback for other head widths and unaligned operands.
 #include <math.h>
 #include <string.h>
+
+#include <algorithm>
 
 #include "sh_internal.cuh"
 
@@ -139,9 +141,10 @@ extern "C" {
 uint32_t sh_attention_l1_bytes_q(uint32_t S, uint32_t dh, uint32_t sq) {
     (void)S;
     (void)sq;
-    // the tensor-core kernel (dh = 64): Q, K, V tiles of 128 x 64 + the 128 x 128 P tile + alignment + barriers;
-    // the CUDA-core kernel: one staged block of 32 keys of K and V in fp32
-    return dh == 64 ? 3 * 128 * 64 * 2 + 128 * 128 * 2 + 1024 + 128 : 2 * kSimtKeys * (dh <= 128 ? dh : 128) * 4;
+    // the tensor-core kernel (dh = 64): two Q slots of two 128 x 64 tiles, three K/V stages of 128 keys, two
+    // 128 x 128 P tiles, barriers and alignment; the CUDA-core kernel: one staged block of 32 keys of K and V in fp32
+    return dh == 64 ? 4 * 128 * 64 * 2 + 3 * 2 * 128 * 64 * 2 + 2 * 128 * 128 * 2 + 256 + 1024
+                    : 2 * kSimtKeys * (dh <= 128 ? dh : 128) * 4;
 }
 
 uint32_t sh_attention_l1_bytes(uint32_t S, uint32_t dh) { return sh_attention_l1_bytes_q(S, dh, S); }
@@ -204,57 +207,77 @@ int sh_cuda_attention_batched(uint64_t q, uint64_t k, uint64_t v, uint64_t o, ui
 }  // extern "C"
 
 // ================================================================================================================
-// Tensor-core path (dh = 64). One CTA per (sequence, head, block of 128 query rows), 160 threads:
-//   warp 0, lane 0 : TMA loads (Q once, K/V block by block) and the tcgen05.mma issue;
-//   warps 1..4     : softmax + output, one query row per thread (warp w owns TMEM lanes 32 (w % 4) ..).
-// Per key block of 128:  S = Q K^T (M=128, N=128, K=64; both K-major) -> TMEM columns [0, 128);
-//   softmax warps read S twice (row max, then exp2 + fp16 P into shared memory in the 128-byte-swizzled K-major
-//   layout the next MMA reads), Opart = P V (M=128, N=64, K=128; V is MN-major as stored) -> TMEM [128, 192);
-//   the running output o = o * exp2(m_old - m_new) + Opart, running max m and sum l stay in registers.
-// Q/K/V are read through 3-D tensor maps [sequence, row, column], so rows past the end of a sequence are zeros;
-// keys past the end are masked to -inf before the softmax. Shared memory: Q 16 KB + K 16 KB + V 16 KB + P 32 KB,
-// tensor memory 256 columns: two CTAs fit on an SM and overlap each other's softmax with their MMAs.
+// Tensor-core path (dh = 64): a persistent, warp-specialised flash-attention kernel.
+// Work item = (sequence b, head h, pair of 128-row query tiles); a CTA per SM walks the items. 320 threads:
+//   warp 0 (one thread)  : TMA loads: the item's two Q tiles into one of two Q slots, K / V blocks of 128 keys into
+//                          a 3-stage ring (separate `full` barriers for K and V, one `empty` barrier per stage);
+//   warp 1 (one thread)  : tcgen05.mma issue. Per key block g: S_t = Q_t K^T (M=128, N=128, K=64) for both tiles t
+//                          into tensor memory, then (one block behind, so the next scores are ready when a softmax
+//                          finishes) O_t (+)= P_t V (M=128, N=64, K=128; P K-major from shared memory, V MN-major);
+//   warps 2..5 / 6..9    : softmax of tile 0 / 1, one query row per thread (warp w reads TMEM lanes 32 (w % 4) ..).
+//                          The 128 scores of a block are loaded into registers at once (S is free for the next block
+//                          right after), the running max m is only raised when a block's max exceeds it by more than
+//                          8 (log2 units; P <= 2^8 then, exact in fp16), in which case O (in tensor memory) is
+//                          rescaled before the next P V accumulates. P = 2^(s sl2 - m) goes to shared memory in the
+//                          128-byte-swizzled K-major layout; l sums the fp16-rounded P that the MMA consumes. At the
+//                          end of an item O / l is staged (swizzled) in the P buffer and leaves by a TMA store.
+// Q/K/V/O are addressed through 3-D tensor maps [sequence, row, column]: rows past the end of a sequence read as zero
+// and are not written; keys past the end are masked to -inf. Tensor memory: S_0, S_1 (128 columns each), O_0, O_1
+// (64 each) in a 512-column allocation. Shared memory: Q 2 x 32 KB, K/V 3 x 32 KB, P 2 x 32 KB.
 // ================================================================================================================
 namespace {
 
 constexpr int kTcRows = 128, kTcKeys = 128, kTcDh = 64;
-constexpr uint32_t kTileBytes = kTcRows * kTcDh * 2;          // 16 KB: Q, K or V tile
-constexpr uint32_t kPBytes = kTcRows * kTcKeys * 2;           // 32 KB: P, two 64-key halves of 16 KB
-constexpr uint32_t kAttnSmem = 3 * kTileBytes + kPBytes + 1024 + 128;
-constexpr uint32_t kAttnTmemCols = 256;
+constexpr int kKvStages = 3;
+constexpr uint32_t kTileBytes = kTcRows * kTcDh * 2;          // 16 KB: one Q, K or V tile
+constexpr uint32_t kPBytes = kTcRows * kTcKeys * 2;           // 32 KB: P of one query tile, two 64-key halves
+constexpr uint32_t kQOff = 0, kKvOff = 4 * kTileBytes, kPOff = kKvOff + kKvStages * 2 * kTileBytes;
+constexpr uint32_t kBarOff = kPOff + 2 * kPBytes;
+constexpr uint32_t kAttnSmem = kBarOff + 256 + 1024;
+constexpr uint32_t kAttnTmemCols = 512;
+constexpr uint32_t kAttnThreads = 320;
+constexpr float kRescaleLog2 = 8.f;
 
 struct AttnArgs {
-    __half *o;
-    uint32_t S, ldo, nkb;
+    uint32_t S, H, nkb, nqp, items;
     float sl2;   // scale * log2(e)
     int *err;
 };
 
-__global__ void __launch_bounds__(160, 2)
+__global__ void __launch_bounds__(kAttnThreads, 1)
     k_attn_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
-              const __grid_constant__ CUtensorMap mv, AttnArgs a) {
+              const __grid_constant__ CUtensorMap mv, const __grid_constant__ CUtensorMap mo, AttnArgs a) {
     extern __shared__ uint8_t smem_raw[];
     const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
     uint8_t *sm = smem_raw + pad;
-    uint8_t *sq = sm, *sk = sm + kTileBytes, *sv = sm + 2 * kTileBytes, *sp = sm + 3 * kTileBytes;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(sm + 3 * kTileBytes + kPBytes);
-    uint64_t *bq = bars, *bkv = bars + 1, *bs = bars + 2, *bp = bars + 3, *bo = bars + 4, *bdone = bars + 5;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 6);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(sm + kBarOff);
+    uint64_t *q_full = bars, *q_empty = bars + 2;
+    uint64_t *k_full = bars + 4, *v_full = k_full + kKvStages, *kv_empty = v_full + kKvStages;
+    uint64_t *s_full = kv_empty + kKvStages, *s_free = s_full + 2, *p_full = s_free + 2, *o_full = p_full + 2;
+    uint64_t *mdone = o_full + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mdone + 1);
     volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t qb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
     if (threadIdx.x == 0) {
-        mbar_init(bq, 1);
-        mbar_init(bkv, 1);
-        mbar_init(bs, 1);
-        mbar_init(bp, 4);
-        mbar_init(bo, 1);
-        mbar_init(bdone, 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&q_full[i], 1);
+            mbar_init(&q_empty[i], 1);
+            mbar_init(&s_full[i], 1);
+            mbar_init(&s_free[i], 4);
+            mbar_init(&p_full[i], 4);
+            mbar_init(&o_full[i], 1);
+        }
+        for (int i = 0; i < kKvStages; ++i) {
+            mbar_init(&k_full[i], 1);
+            mbar_init(&v_full[i], 1);
+            mbar_init(&kv_empty[i], 1);
+        }
+        mbar_init(mdone, 1);
         *abort = 0;
         fence_mbar_init();
     }
-    if (warp == 0) {
+    if (warp == 1) {
         tmem_alloc(tmem_slot, kAttnTmemCols);
         tmem_relinquish();
     }
@@ -262,162 +285,274 @@ __global__ void __launch_bounds__(160, 2)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const int32_t col = (int32_t)(h * kTcDh);
 
     if (warp == 0) {
         if (lane == 0) {
+            // ---------------- TMA producer ----------------
             prefetch_tmap(&mq);
             prefetch_tmap(&mk);
             prefetch_tmap(&mv);
+            uint32_t qs = 0, qph = 0, st = 0, kph = 0;
+            uint32_t q_armed[2] = {2, 2}, kv_armed[kKvStages];
+            for (int i = 0; i < kKvStages; ++i) kv_armed[i] = 2;
+            bool ok = true;
+            for (uint32_t it = blockIdx.x; ok && it < a.items; it += gridDim.x) {
+                const uint32_t qp = it % a.nqp, bh = it / a.nqp;
+                const int32_t col = (int32_t)((bh % a.H) * kTcDh), b = (int32_t)(bh / a.H);
+                if (!mbar_wait(&q_empty[qs], qph ^ 1u, abort, a.err)) break;
+                mbar_arrive_expect_tx(&q_full[qs], 2 * kTileBytes);
+                q_armed[qs] = qph;
+                uint8_t *q0 = sm + kQOff + qs * 2 * kTileBytes;
+                tma_load_3d(q0, &mq, &q_full[qs], col, (int32_t)(qp * 2 * kTcRows), b);
+                tma_load_3d(q0 + kTileBytes, &mq, &q_full[qs], col, (int32_t)(qp * 2 * kTcRows + kTcRows), b);
+                if (++qs == 2) {
+                    qs = 0;
+                    qph ^= 1u;
+                }
+                for (uint32_t j = 0; j < a.nkb; ++j) {
+                    if (!mbar_wait(&kv_empty[st], kph ^ 1u, abort, a.err)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t *kt = sm + kKvOff + st * 2 * kTileBytes;
+                    mbar_arrive_expect_tx(&k_full[st], kTileBytes);
+                    tma_load_3d(kt, &mk, &k_full[st], col, (int32_t)(j * kTcKeys), b);
+                    mbar_arrive_expect_tx(&v_full[st], kTileBytes);
+                    tma_load_3d(kt + kTileBytes, &mv, &v_full[st], col, (int32_t)(j * kTcKeys), b);
+                    kv_armed[st] = kph;
+                    if (++st == kKvStages) {
+                        st = 0;
+                        kph ^= 1u;
+                    }
+                }
+            }
+            // drain: every armed load must have landed before the CTA may exit
+            for (int i = 0; i < 2; ++i)
+                if (q_armed[i] != 2) drain_wait(&q_full[i], q_armed[i]);
+            for (int i = 0; i < kKvStages; ++i)
+                if (kv_armed[i] != 2) {
+                    drain_wait(&k_full[i], kv_armed[i]);
+                    drain_wait(&v_full[i], kv_armed[i]);
+                }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ---------------- MMA issuer ----------------
             constexpr uint32_t idesc_s = umma_idesc_f16(kTcRows, kTcKeys, 0, 0);
             constexpr uint32_t idesc_o = umma_idesc_f16(kTcRows, kTcDh, 0, 1);
-            mbar_arrive_expect_tx(bq, kTileBytes);
-            tma_load_3d(sq, &mq, bq, col, (int32_t)(qb * kTcRows), (int32_t)b);
-            bool q_landed = false, kv_armed = false, ok = true;
-            uint32_t kv_phase = 0;
-            for (uint32_t j = 0; ok && j < a.nkb; ++j) {
-                const uint32_t ph = j & 1u;
-                if (j > 0 && !mbar_wait(bo, ph ^ 1u, abort, a.err)) break;   // P V of block j-1 done with V, P
-                mbar_arrive_expect_tx(bkv, 2 * kTileBytes);
-                kv_armed = true;
-                kv_phase = ph;
-                tma_load_3d(sk, &mk, bkv, col, (int32_t)(j * kTcKeys), (int32_t)b);
-                tma_load_3d(sv, &mv, bkv, col, (int32_t)(j * kTcKeys), (int32_t)b);
-                if (!q_landed) {
-                    if (!mbar_wait(bq, 0, abort, a.err)) break;
-                    q_landed = true;
-                }
-                if (!mbar_wait(bkv, ph, abort, a.err)) break;
-                tc_fence_after();
-                const uint32_t aq = smem_u32(sq), ak = smem_u32(sk), av = smem_u32(sv), ap = smem_u32(sp);
+            const uint32_t p_addr = smem_u32(sm + kPOff);
+            uint32_t qs = 0, qph = 0, st = 0, kph = 0, g = 0;
+            // the P V of the previous block: its stage, block counter and whether it opens an item
+            bool have_prev = false, prev_first = false;
+            uint32_t prev_st = 0, prev_ph = 0, prev_g = 0;
+            bool ok = true;
+            auto issue_pv = [&](uint32_t pst, uint32_t pph, uint32_t pg, bool first) -> bool {
+                if (!mbar_wait(&v_full[pst], pph, abort, a.err)) return false;
+                const uint32_t av = smem_u32(sm + kKvOff + pst * 2 * kTileBytes + kTileBytes);
+#pragma unroll 1
+                for (uint32_t t = 0; t < 2; ++t) {
+                    if (!mbar_wait(&p_full[t], pg & 1u, abort, a.err)) return false;
+                    tc_fence_after();
+                    const uint32_t ap = p_addr + t * kPBytes;
 #pragma unroll
-                for (int k = 0; k < kTcDh / 16; ++k)
-                    umma_f16_ss(tmem, sw128_desc(aq + k * 32, 16, 1024), sw128_desc(ak + k * 32, 16, 1024), idesc_s,
-                                k > 0 ? 1u : 0u);
-                umma_commit(bs);
-                if (!mbar_wait(bp, ph, abort, a.err)) {
+                    for (int k = 0; k < kTcKeys / 16; ++k)
+                        umma_f16_ss(tmem + 256 + t * kTcDh,
+                                    sw128_desc(ap + (k >> 2) * (kTcRows * 128) + (k & 3) * 32, 16, 1024),
+                                    sw128_desc(av + k * 2048, 16384, 1024), idesc_o, (first && k == 0) ? 0u : 1u);
+                    umma_commit(&o_full[t]);
+                }
+                umma_commit(&kv_empty[pst]);
+                return true;
+            };
+            for (uint32_t it = blockIdx.x; ok && it < a.items; it += gridDim.x) {
+                if (!mbar_wait(&q_full[qs], qph, abort, a.err)) break;
+                const uint32_t aq = smem_u32(sm + kQOff + qs * 2 * kTileBytes);
+                for (uint32_t j = 0; j < a.nkb; ++j) {
+                    if (!mbar_wait(&k_full[st], kph, abort, a.err)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t ak = smem_u32(sm + kKvOff + st * 2 * kTileBytes);
+#pragma unroll 1
+                    for (uint32_t t = 0; t < 2 && ok; ++t) {
+                        // the softmax of tile t has its previous scores in registers
+                        if (!mbar_wait(&s_free[t], (g & 1u) ^ 1u, abort, a.err)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+#pragma unroll
+                        for (int k = 0; k < kTcDh / 16; ++k)
+                            umma_f16_ss(tmem + t * kTcKeys, sw128_desc(aq + t * kTileBytes + k * 32, 16, 1024),
+                                        sw128_desc(ak + k * 32, 16, 1024), idesc_s, k > 0 ? 1u : 0u);
+                        umma_commit(&s_full[t]);
+                    }
+                    if (!ok) break;
+                    if (j + 1 == a.nkb) umma_commit(&q_empty[qs]);   // Q slot free once these MMAs complete
+                    if (have_prev && !issue_pv(prev_st, prev_ph, prev_g, prev_first)) {
+                        ok = false;
+                        break;
+                    }
+                    have_prev = true;
+                    prev_first = j == 0;
+                    prev_st = st;
+                    prev_ph = kph;
+                    prev_g = g;
+                    ++g;
+                    if (++st == kKvStages) {
+                        st = 0;
+                        kph ^= 1u;
+                    }
+                }
+                if (++qs == 2) {
+                    qs = 0;
+                    qph ^= 1u;
+                }
+            }
+            if (ok && have_prev) issue_pv(prev_st, prev_ph, prev_g, prev_first);
+            // exit path: tensor memory may only be freed once every issued MMA has completed
+            umma_commit(mdone);
+            drain_wait(mdone, 0);
+        }
+    } else {
+        // ---------------- softmax + output (warps 2..5: tile 0, warps 6..9: tile 1) ----------------
+        const uint32_t t = (warp - 2u) >> 2;
+        const uint32_t quarter = warp & 3u;
+        const uint32_t r = quarter * 32 + lane;                  // query row within the tile
+        const uint32_t lane_base = tmem + ((quarter * 32u) << 16);
+        const uint32_t s_addr = lane_base + t * kTcKeys, o_addr = lane_base + 256 + t * kTcDh;
+        uint8_t *pt = sm + kPOff + t * kPBytes;
+        uint8_t *prow = pt + r * 128;
+        uint32_t g = 0;
+        bool store_pending = false, ok = true;
+        for (uint32_t it = blockIdx.x; ok && it < a.items; it += gridDim.x) {
+            float m = -INFINITY, l = 0.f;
+            for (uint32_t j = 0; j < a.nkb; ++j, ++g) {
+                if (!mbar_wait(&s_full[t], g & 1u, abort, a.err)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
+                float sc[kTcKeys];
+                {
+                    uint32_t v[32];
 #pragma unroll
-                for (int k = 0; k < kTcKeys / 16; ++k)
-                    umma_f16_ss(tmem + kTcKeys,
-                                sw128_desc(ap + (k >> 2) * (kTcRows * 128) + (k & 3) * 32, 16, 1024),
-                                sw128_desc(av + k * 2048, 16384, 1024), idesc_o, k > 0 ? 1u : 0u);
-                umma_commit(bo);
-            }
-            // exit: every issued MMA complete, every issued TMA landed
-            umma_commit(bdone);
-            const long long t0 = clock64();
-            while (!mbar_try_wait(bdone, 0) && (unsigned long long)(clock64() - t0) < SH_SPIN_CYCLES) {
-            }
-            if (kv_armed)
-                while (!mbar_try_wait(bkv, kv_phase) && (unsigned long long)(clock64() - t0) < 2 * SH_SPIN_CYCLES) {
-                }
-            if (!q_landed)
-                while (!mbar_try_wait(bq, 0) && (unsigned long long)(clock64() - t0) < 3 * SH_SPIN_CYCLES) {
-                }
-        }
-    } else {
-        // ---------------- softmax + output (warps 1..4) ----------------
-        const uint32_t quarter = warp & 3u;
-        const uint32_t r = quarter * 32 + lane;                 // query row within the tile
-        const uint32_t lane_addr = tmem + ((quarter * 32u) << 16);
-        float o[kTcDh];
+                    for (int c = 0; c < kTcKeys / 32; ++c) {
+                        tmem_ld_32x32b_x32(s_addr + c * 32, v);
+                        tmem_ld_wait();
 #pragma unroll
-        for (int d = 0; d < kTcDh; ++d) o[d] = 0.f;
-        float m = -INFINITY, l = 0.f;
-        bool ok = true;
-        for (uint32_t j = 0; j < a.nkb; ++j) {
-            const uint32_t ph = j & 1u;
-            if (!mbar_wait(bs, ph, abort, a.err)) {
-                ok = false;
-                break;
-            }
-            tc_fence_after();
-            const int32_t valid = (int32_t)a.S - (int32_t)(j * kTcKeys);   // keys of this block inside the sequence
-            // pass 1: row max of the scaled scores
-            float mb = -INFINITY;
+                        for (int i = 0; i < 32; ++i) sc[c * 32 + i] = __uint_as_float(v[i]);
+                    }
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&s_free[t]);
+                const int32_t valid = (int32_t)a.S - (int32_t)(j * kTcKeys);
+                if (valid < kTcKeys) {
+#pragma unroll
+                    for (int i = 0; i < kTcKeys; ++i)
+                        if (i >= valid) sc[i] = -INFINITY;
+                }
+                float mb = sc[0];
+#pragma unroll
+                for (int i = 1; i < kTcKeys; ++i) mb = fmaxf(mb, sc[i]);
+                mb *= a.sl2;
+                // P V of the previous block is done: P's buffer and O may be touched
+                if (j > 0 && !mbar_wait(&o_full[t], (g - 1u) & 1u, abort, a.err)) {
+                    ok = false;
+                    break;
+                }
+                // the running max only moves when this block's max exceeds it by more than kRescaleLog2
+                float alpha = 1.f;
+                bool raise = false;
+                if (j == 0) {
+                    m = mb;
+                } else if (mb > m + kRescaleLog2) {
+                    raise = true;
+                    alpha = fast_exp2(m - mb);
+                    l *= alpha;
+                    m = mb;
+                }
+                if (store_pending) {   // the previous item's O is still being read out of this buffer
+                    if (lane == 0) bulk_wait_read0();
+                    __syncwarp();
+                    store_pending = false;
+                }
+                float ls = 0.f;
+#pragma unroll
+                for (int u = 0; u < kTcKeys / 8; ++u) {
+                    uint32_t packed[4];
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const float p0 = fast_exp2(fmaf(sc[8 * u + 2 * i], a.sl2, -m));
+                        const float p1 = fast_exp2(fmaf(sc[8 * u + 2 * i + 1], a.sl2, -m));
+                        const __half2 hp = __floats2half2_rn(p0, p1);
+                        const float2 back = __half22float2(hp);
+                        ls += back.x + back.y;
+                        packed[i] = *reinterpret_cast<const uint32_t *>(&hp);
+                    }
+                    // key unit u (8 keys) lives in half (u >> 3) at unit (u & 7) ^ (r & 7) of row r
+                    *reinterpret_cast<uint4 *>(prow + (u >> 3) * (kTcRows * 128) + (((u & 7u) ^ (r & 7u)) * 16)) =
+                        make_uint4(packed[0], packed[1], packed[2], packed[3]);
+                }
+                l += ls;
+                if (__any_sync(0xffffffffu, raise)) {   // O *= alpha before the next P V accumulates into it
+                    tc_fence_after();
 #pragma unroll 1
-            for (int c = 0; c < kTcKeys / 32; ++c) {
-                uint32_t v[32];
-                tmem_ld_32x32b_x32(lane_addr + c * 32, v);
-                tmem_ld_wait();
+                    for (int c = 0; c < kTcDh / 32; ++c) {
+                        uint32_t v[32];
+                        tmem_ld_32x32b_x32(o_addr + c * 32, v);
+                        tmem_ld_wait();
 #pragma unroll
-                for (int i = 0; i < 32; ++i)
-                    if (c * 32 + i < valid) mb = fmaxf(mb, __uint_as_float(v[i]) * a.sl2);
-            }
-            const float mn = fmaxf(m, mb);
-            const float alpha = fast_exp2(m - mn);
-            // pass 2: p = 2^(s sl2 - mn) -> fp16 into the swizzled P tile; l accumulates the rounded values
-            float ls = 0.f;
-            uint8_t *prow = sp + r * 128;
-#pragma unroll 1
-            for (int c = 0; c < kTcKeys / 32; ++c) {
-                uint32_t v[32];
-                tmem_ld_32x32b_x32(lane_addr + c * 32, v);
-                tmem_ld_wait();
-                uint32_t packed[16];
-#pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    const int k0 = c * 32 + 2 * i;
-                    const float p0 = (k0 < valid) ? fast_exp2(__uint_as_float(v[2 * i]) * a.sl2 - mn) : 0.f;
-                    const float p1 = (k0 + 1 < valid) ? fast_exp2(__uint_as_float(v[2 * i + 1]) * a.sl2 - mn) : 0.f;
-                    const __half2 hp = __floats2half2_rn(p0, p1);
-                    const float2 back = __half22float2(hp);
-                    ls += back.x + back.y;
-                    packed[i] = *reinterpret_cast<const uint32_t *>(&hp);
+                        for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
+                        tmem_st_32x32b_x32(o_addr + c * 32, v);
+                    }
+                    tmem_st_wait();
                 }
-                // 32 keys = 4 units of 16 B; key unit u (0..15 over the row) lives in half (u >> 3) at unit
-                // (u & 7) ^ (r & 7) of row r
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const uint32_t u = c * 4 + q;
-                    uint8_t *dst = prow + (u >> 3) * (kTcRows * 128) + (((u & 7u) ^ (r & 7u)) * 16);
-                    *reinterpret_cast<uint4 *>(dst) =
-                        make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
-                }
+                fence_proxy_async_smem();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&p_full[t]);
             }
-            l = l * alpha + ls;
-            m = mn;
-            fence_proxy_async_smem();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(bp);
-            if (!mbar_wait(bo, ph, abort, a.err)) {
-                ok = false;
-                break;
-            }
+            if (!ok) break;
+            // ---- item epilogue: O / l -> fp16, staged in this warp's 32 rows of P's first half, one TMA store ----
+            if (!mbar_wait(&o_full[t], (g - 1u) & 1u, abort, a.err)) break;
             tc_fence_after();
+            const float inv = 1.f / l;
 #pragma unroll
             for (int c = 0; c < kTcDh / 32; ++c) {
                 uint32_t v[32];
-                tmem_ld_32x32b_x32(lane_addr + kTcKeys + c * 32, v);
+                tmem_ld_32x32b_x32(o_addr + c * 32, v);
                 tmem_ld_wait();
 #pragma unroll
-                for (int i = 0; i < 32; ++i) o[c * 32 + i] = o[c * 32 + i] * alpha + __uint_as_float(v[i]);
+                for (int q = 0; q < 4; ++q) {
+                    uint4 out;
+                    __half2 *hh = reinterpret_cast<__half2 *>(&out);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i)
+                        hh[i] = __floats2half2_rn(__uint_as_float(v[8 * q + 2 * i]) * inv,
+                                                  __uint_as_float(v[8 * q + 2 * i + 1]) * inv);
+                    const uint32_t u = c * 4 + q;
+                    *reinterpret_cast<uint4 *>(prow + ((u ^ (r & 7u)) * 16)) = out;
+                }
             }
             tc_fence_before();
-        }
-        const uint32_t row = qb * kTcRows + r;
-        if (ok && row < a.S) {
-            const float inv = 1.f / l;
-            __half *dst = a.o + ((size_t)b * a.S + row) * a.ldo + (size_t)h * kTcDh;
-#pragma unroll
-            for (int q = 0; q < kTcDh / 8; ++q) {
-                uint4 out;
-                __half2 *hh = reinterpret_cast<__half2 *>(&out);
-#pragma unroll
-                for (int i = 0; i < 4; ++i) hh[i] = __floats2half2_rn(o[8 * q + 2 * i] * inv, o[8 * q + 2 * i + 1] * inv);
-                *reinterpret_cast<uint4 *>(dst + 8 * q) = out;
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                const uint32_t qp = it % a.nqp, bh = it / a.nqp;
+                tma_store_3d(&mo, pt + quarter * 32 * 128, (int32_t)((bh % a.H) * kTcDh),
+                             (int32_t)(qp * 2 * kTcRows + t * kTcRows + quarter * 32), (int32_t)(bh / a.H));
+                bulk_commit();
             }
+            store_pending = true;
         }
+        if (lane == 0) bulk_wait_all();
     }
     __syncwarp();
     tc_fence_before();
     __syncthreads();
-    if (warp == 0) {
+    if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem, kAttnTmemCols);
     }
@@ -434,10 +569,11 @@ int attention_tc_launch(const __half *q, const __half *k, const __half *v, __hal
         !aligned16((uint64_t)o) || ldq % 8 || ldk % 8 || ldv % 8 || ldo % 8 || !encode_tiled())
         return 0;   // the CUDA-core kernel handles it
     const uint64_t cols_q = (uint64_t)H * dh;
-    CUtensorMap mq, mk, mv;
+    CUtensorMap mq, mk, mv, mo;
     if (!make_map_3d(&mq, q, B, S, cols_q, ldq, (uint64_t)S * ldq, kTcRows, kTcDh) ||
         !make_map_3d(&mk, k, B, S, cols_q, ldk, (uint64_t)S * ldk, kTcKeys, kTcDh) ||
-        !make_map_3d(&mv, v, B, S, cols_q, ldv, (uint64_t)S * ldv, kTcKeys, kTcDh))
+        !make_map_3d(&mv, v, B, S, cols_q, ldv, (uint64_t)S * ldv, kTcKeys, kTcDh) ||
+        !make_map_3d(&mo, o, B, S, cols_q, ldo, (uint64_t)S * ldo, 32, kTcDh))
         return 0;
     static bool attr_done[kMaxDevices] = {};
     const int dev = current_device() % kMaxDevices;
@@ -448,15 +584,17 @@ int attention_tc_launch(const __half *q, const __half *k, const __half *v, __hal
         attr_done[dev] = true;
     }
     AttnArgs a;
-    a.o = o;
     a.S = S;
-    a.ldo = ldo;
+    a.H = H;
     a.nkb = (S + kTcKeys - 1) / kTcKeys;
+    a.nqp = (S + 2 * kTcRows - 1) / (2 * kTcRows);
+    const uint64_t items = (uint64_t)B * H * a.nqp;
+    if (items > 0xffffffffull) return 0;
+    a.items = (uint32_t)items;
     a.sl2 = scale * 1.4426950408889634f;
     a.err = state().dev_err;
-    dim3 grid((S + kTcRows - 1) / kTcRows, H, B);
-    if (grid.y > 65535u || grid.z > 65535u) return 0;
-    k_attn_tc<<<grid, 160, kAttnSmem, stream()>>>(mq, mk, mv, a);
+    const uint32_t grid = (uint32_t)std::min<uint64_t>(items, (uint64_t)state().num_sms);
+    k_attn_tc<<<grid, kAttnThreads, kAttnSmem, stream()>>>(mq, mk, mv, mo, a);
     *launched = true;
     return cuda_ok(cudaGetLastError(), "sh_attention") ? 0 : -1;
 }

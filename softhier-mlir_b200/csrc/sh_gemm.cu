@@ -65,13 +65,6 @@ __device__ __forceinline__ bool epi_sync(uint64_t *bar, uint32_t &phase, volatil
     return ok;
 }
 
-// Bounded wait that ignores the abort flag: used to drain outstanding asynchronous work before exit.
-__device__ __forceinline__ void drain_wait(uint64_t *bar, uint32_t parity) {
-    const long long t0 = clock64();
-    while (!mbar_try_wait(bar, parity))
-        if ((unsigned long long)(clock64() - t0) > SH_SPIN_CYCLES) break;
-}
-
 // fused epilogue of 8 consecutive columns of one row (values in v, fp32). Z is fp16, or fp32 with SH_EPI_F32_OUT;
 // SH_EPI_ACC_F32_IN adds an fp32 matrix passed as `resid` (leading dim ldr) instead of an fp16 residual.
 __device__ __forceinline__ void epilogue8(const GemmArgs &a, uint32_t row, uint32_t col, float (&v)[8]) {
