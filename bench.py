@@ -1,7 +1,7 @@
 #!/usr/bin/env python3
 """Headline benchmark: SigLIP-base encoder images/s on B200 through libsh_ops_cuda.so.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload encoder|gemm512|gemm|rowops|summa]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload encoder|gemm512|gemm|attention|rowops|summa]
 
 Workload: 12 pre-LN SigLIP-base layers (S=256, D=768, 12 heads x 64, FFN 3072, tanh-GELU,
 scale 1/8, eps 1e-6), a global batch of 512 sequences sharded data-parallel over the N ranks (B = 512 / N per GPU,
@@ -484,6 +484,39 @@ def run_gemm(args, local: int) -> dict:
                        "l2": "Z alone larger than L2 at the default shape; no flush"}}
 
 
+def run_attention(args, local: int) -> dict:
+    """The encoder's attention launch alone (`--attn B,S,H`, dh = 64, packed q|k|v with ld 3 D as the encoder stores
+    them): per-launch time and TFLOP/s (4 B S^2 D). q, k, v N(0, 1); the output is larger than L2 at B = 512."""
+    import torch
+    from softhier_cuda.runtime import Runtime
+    B, S, H = (int(v) for v in args.attn.split(","))
+    D = 64 * H
+    M = B * S
+    rt = Runtime.open(local, arena_bytes=2 * (M * 3 * D + M * D) + (64 << 20))
+    lib = rt.lib
+    qkv, o = rt.alloc(M, 3 * D), rt.alloc(M, D)
+    lib.sh_cuda_fill_normal_fp16(qkv, M, 3 * D, 3 * D, 7, 0.0, 1.0)
+    stream = torch.cuda.Stream(device=local)
+    rt.activate(stream)
+    call = lambda: lib.sh_cuda_attention_batched(qkv, qkv + 2 * D, qkv + 4 * D, o, S, D, H, 3 * D, 3 * D, 3 * D, D,  # noqa: E731
+                                                 0.125, B)
+    with torch.cuda.stream(stream):
+        for _ in range(max(3, args.warmup)):
+            if call():
+                raise RuntimeError(lib.sh_cuda_last_error_string().decode())
+        rt.check()
+        ms = _event_time(torch, stream, call, max(1, args.steps))
+    rt.check()
+    flop = 4.0 * B * S * S * D
+    pk, src = peaks()
+    tf = flop / ms / 1e9
+    return {"metric": "attention TFLOP/s", "value": round(tf, 1), "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "dtype": "f16",
+            "frac_of_peak": round(tf / pk["bf16_tflops"], 4), "peak": f"{src} bf16 burst {pk['bf16_tflops']} TFLOP/s",
+            "exp_per_s": round(B * H * S * S / (ms * 1e-3) / 1e12, 3),
+            "config": {"workload": f"sh_cuda_attention_batched B={B} S={S} H={H} dh=64 (packed qkv, ld {3 * D})"}}
+
+
 def run_rowops(args, local: int) -> dict:
     """Config 2 at the HBM-resident activation shape of config 5 (131072 rows x 768 / 3072): per-op GB/s, rotating
     over buffers that total more than twice the L2 so every launch streams from HBM."""
@@ -618,7 +651,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-images", type=int, default=2)
     ap.add_argument("--debug", action="store_true")
-    ap.add_argument("--workload", choices=["encoder", "gemm512", "gemm", "rowops", "summa"], default="encoder")
+    ap.add_argument("--workload", choices=["encoder", "gemm512", "gemm", "attention", "rowops", "summa"],
+                    default="encoder")
+    ap.add_argument("--attn", default="512,256,12", help="B,S,H of --workload attention")
     ap.add_argument("--gemm", default="131072,3072,768", help="M,N,K of --workload gemm")
     ap.add_argument("--epi", default="bias,gelu", help="fused epilogue of --workload gemm: bias,gelu,residual")
     ap.add_argument("--summa-n", type=int, default=16384)
@@ -630,6 +665,8 @@ def main():
         out = run_gemm512(args, local) if rank == 0 else None
     elif args.workload == "gemm":
         out = run_gemm(args, local) if rank == 0 else None
+    elif args.workload == "attention":
+        out = run_attention(args, local) if rank == 0 else None
     elif args.workload == "rowops":
         out = run_rowops(args, local) if rank == 0 else None
     elif args.workload == "summa":

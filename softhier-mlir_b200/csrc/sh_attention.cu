@@ -212,15 +212,17 @@ int sh_cuda_attention_batched(uint64_t q, uint64_t k, uint64_t v, uint64_t o, ui
 //   warp 0 (one thread)  : TMA loads: the item's two Q tiles into one of two Q slots, K / V blocks of 128 keys into
 //                          a 3-stage ring (separate `full` barriers for K and V, one `empty` barrier per stage);
 //   warp 1 (one thread)  : tcgen05.mma issue. Per key block g: S_t = Q_t K^T (M=128, N=128, K=64) for both tiles t
-//                          into tensor memory, then (one block behind, so the next scores are ready when a softmax
-//                          finishes) O_t (+)= P_t V (M=128, N=64, K=128; P K-major from shared memory, V MN-major);
+//                          into tensor memory as soon as each softmax holds its previous scores, then (one block
+//                          behind, so the next scores are ready when a softmax finishes) O_t (+)= P_t V (M=128, N=64,
+//                          K=128; P K-major from shared memory, V MN-major). (One issuer thread per tile measured
+//                          6 % slower at B = 512, S = 256.)
 //   warps 2..5 / 6..9    : softmax of tile 0 / 1, one query row per thread (warp w reads TMEM lanes 32 (w % 4) ..).
 //                          The 128 scores of a block are loaded into registers at once (S is free for the next block
 //                          right after), the running max m is only raised when a block's max exceeds it by more than
 //                          8 (log2 units; P <= 2^8 then, exact in fp16), in which case O (in tensor memory) is
 //                          rescaled before the next P V accumulates. P = 2^(s sl2 - m) goes to shared memory in the
-//                          128-byte-swizzled K-major layout; l sums the fp16-rounded P that the MMA consumes. At the
-//                          end of an item O / l is staged (swizzled) in the P buffer and leaves by a TMA store.
+//                          128-byte-swizzled K-major layout (fp16); l sums P in fp32. At the end of an item O / l is
+//                          staged (swizzled) in the P buffer and leaves by a TMA store.
 // Q/K/V/O are addressed through 3-D tensor maps [sequence, row, column]: rows past the end of a sequence read as zero
 // and are not written; keys past the end are masked to -inf. Tensor memory: S_0, S_1 (128 columns each), O_0, O_1
 // (64 each) in a 512-column allocation. Shared memory: Q 2 x 32 KB, K/V 3 x 32 KB, P 2 x 32 KB.
@@ -237,6 +239,20 @@ constexpr uint32_t kAttnSmem = kBarOff + 256 + 1024;
 constexpr uint32_t kAttnTmemCols = 512;
 constexpr uint32_t kAttnThreads = 320;
 constexpr float kRescaleLog2 = 8.f;
+constexpr int kDefaultPoly = 0;
+
+// 2^x on the FMA pipe, for x <= 16 (a share of the softmax exponentials is computed here instead of on the special
+// function unit, which otherwise bounds the softmax): x = n + f with n = round(x) (by the 1.5 * 2^23 addition trick)
+// and f in [-0.5, 0.5]; 2^f by a cubic whose coefficients were fit for minimal relative error on [-0.5, 0.5] by
+// Lawson-weighted least squares (max relative error 7.5e-5, below half an fp16 ulp); 2^n is added to the exponent
+// field. x is clamped at -126 so that the result stays a (sub)normal positive number; P rounds to fp16 zero there.
+__device__ __forceinline__ float exp2_poly(float x) {
+    x = fmaxf(x, -126.f);
+    const float t = x + 12582912.f;
+    const float f = x - (t - 12582912.f);
+    const float p = fmaf(fmaf(fmaf(0.0551716685f, f, 0.2426111400f), f, 0.6932609677f), f, 0.9999280572f);
+    return __int_as_float(__float_as_int(p) + ((__float_as_int(t) - 0x4B400000) << 23));
+}
 
 struct AttnArgs {
     uint32_t S, H, nkb, nqp, items;
@@ -244,6 +260,8 @@ struct AttnArgs {
     int *err;
 };
 
+// POLY of every 8 consecutive keys take exp2_poly, the rest the special function unit
+template <int POLY>
 __global__ void __launch_bounds__(kAttnThreads, 1)
     k_attn_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
               const __grid_constant__ CUtensorMap mv, const __grid_constant__ CUtensorMap mo, AttnArgs a) {
@@ -254,15 +272,16 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     uint64_t *q_full = bars, *q_empty = bars + 2;
     uint64_t *k_full = bars + 4, *v_full = k_full + kKvStages, *kv_empty = v_full + kKvStages;
     uint64_t *s_full = kv_empty + kKvStages, *s_free = s_full + 2, *p_full = s_free + 2, *o_full = p_full + 2;
-    uint64_t *mdone = o_full + 2;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mdone + 1);
+    uint64_t *mdone = o_full + 2;   // [2], one per issuer
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mdone + 2);
     volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
         for (int i = 0; i < 2; ++i) {
             mbar_init(&q_full[i], 1);
-            mbar_init(&q_empty[i], 1);
+            mbar_init(&q_empty[i], 1);    // both issuers' commits
+            mbar_init(&mdone[i], 1);
             mbar_init(&s_full[i], 1);
             mbar_init(&s_free[i], 4);
             mbar_init(&p_full[i], 4);
@@ -271,9 +290,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         for (int i = 0; i < kKvStages; ++i) {
             mbar_init(&k_full[i], 1);
             mbar_init(&v_full[i], 1);
-            mbar_init(&kv_empty[i], 1);
+            mbar_init(&kv_empty[i], 1);   // both issuers' commits
         }
-        mbar_init(mdone, 1);
         *abort = 0;
         fence_mbar_init();
     }
@@ -411,8 +429,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             }
             if (ok && have_prev) issue_pv(prev_st, prev_ph, prev_g, prev_first);
             // exit path: tensor memory may only be freed once every issued MMA has completed
-            umma_commit(mdone);
-            drain_wait(mdone, 0);
+            umma_commit(&mdone[0]);
+            drain_wait(&mdone[0], 0);
         }
     } else {
         // ---------------- softmax + output (warps 2..5: tile 0, warps 6..9: tile 1) ----------------
@@ -435,13 +453,18 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                 tc_fence_after();
                 float sc[kTcKeys];
                 {
-                    uint32_t v[32];
+                    uint32_t v0[32], v1[32], v2[32], v3[32];   // four loads in flight, one wait
+                    tmem_ld_32x32b_x32(s_addr, v0);
+                    tmem_ld_32x32b_x32(s_addr + 32, v1);
+                    tmem_ld_32x32b_x32(s_addr + 64, v2);
+                    tmem_ld_32x32b_x32(s_addr + 96, v3);
+                    tmem_ld_wait();
 #pragma unroll
-                    for (int c = 0; c < kTcKeys / 32; ++c) {
-                        tmem_ld_32x32b_x32(s_addr + c * 32, v);
-                        tmem_ld_wait();
-#pragma unroll
-                        for (int i = 0; i < 32; ++i) sc[c * 32 + i] = __uint_as_float(v[i]);
+                    for (int i = 0; i < 32; ++i) {
+                        sc[i] = __uint_as_float(v0[i]);
+                        sc[32 + i] = __uint_as_float(v1[i]);
+                        sc[64 + i] = __uint_as_float(v2[i]);
+                        sc[96 + i] = __uint_as_float(v3[i]);
                     }
                 }
                 tc_fence_before();
@@ -453,16 +476,20 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                     for (int i = 0; i < kTcKeys; ++i)
                         if (i >= valid) sc[i] = -INFINITY;
                 }
-                float mb = sc[0];
+                // row max: eight independent chains, then a tree (a single chain would serialise 127 dependent ops)
+                float mx[8];
 #pragma unroll
-                for (int i = 1; i < kTcKeys; ++i) mb = fmaxf(mb, sc[i]);
+                for (int i = 0; i < 8; ++i) mx[i] = sc[i];
+#pragma unroll
+                for (int i = 8; i < kTcKeys; ++i) mx[i & 7] = fmaxf(mx[i & 7], sc[i]);
+                float mb = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                                 fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
                 mb *= a.sl2;
                 // P V of the previous block is done: P's buffer and O may be touched
                 if (j > 0 && !mbar_wait(&o_full[t], (g - 1u) & 1u, abort, a.err)) {
                     ok = false;
                     break;
                 }
-                // the running max only moves when this block's max exceeds it by more than kRescaleLog2
                 float alpha = 1.f;
                 bool raise = false;
                 if (j == 0) {
@@ -473,29 +500,30 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                     l *= alpha;
                     m = mb;
                 }
-                if (store_pending) {   // the previous item's O is still being read out of this buffer
+                if (store_pending) {
                     if (lane == 0) bulk_wait_read0();
                     __syncwarp();
                     store_pending = false;
                 }
-                float ls = 0.f;
+                float ls8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
                 for (int u = 0; u < kTcKeys / 8; ++u) {
                     uint32_t packed[4];
 #pragma unroll
                     for (int i = 0; i < 4; ++i) {
-                        const float p0 = fast_exp2(fmaf(sc[8 * u + 2 * i], a.sl2, -m));
-                        const float p1 = fast_exp2(fmaf(sc[8 * u + 2 * i + 1], a.sl2, -m));
+                        const float x0 = fmaf(sc[8 * u + 2 * i], a.sl2, -m);
+                        const float x1 = fmaf(sc[8 * u + 2 * i + 1], a.sl2, -m);
+                        const float p0 = (2 * i < POLY) ? exp2_poly(x0) : fast_exp2(x0);
+                        const float p1 = (2 * i + 1 < POLY) ? exp2_poly(x1) : fast_exp2(x1);
+                        ls8[2 * i] += p0;
+                        ls8[2 * i + 1] += p1;
                         const __half2 hp = __floats2half2_rn(p0, p1);
-                        const float2 back = __half22float2(hp);
-                        ls += back.x + back.y;
                         packed[i] = *reinterpret_cast<const uint32_t *>(&hp);
                     }
-                    // key unit u (8 keys) lives in half (u >> 3) at unit (u & 7) ^ (r & 7) of row r
                     *reinterpret_cast<uint4 *>(prow + (u >> 3) * (kTcRows * 128) + (((u & 7u) ^ (r & 7u)) * 16)) =
                         make_uint4(packed[0], packed[1], packed[2], packed[3]);
                 }
-                l += ls;
+                l += ((ls8[0] + ls8[1]) + (ls8[2] + ls8[3])) + ((ls8[4] + ls8[5]) + (ls8[6] + ls8[7]));
                 if (__any_sync(0xffffffffu, raise)) {   // O *= alpha before the next P V accumulates into it
                     tc_fence_after();
 #pragma unroll 1
@@ -575,13 +603,19 @@ int attention_tc_launch(const __half *q, const __half *k, const __half *v, __hal
         !make_map_3d(&mv, v, B, S, cols_q, ldv, (uint64_t)S * ldv, kTcKeys, kTcDh) ||
         !make_map_3d(&mo, o, B, S, cols_q, ldo, (uint64_t)S * ldo, 32, kTcDh))
         return 0;
-    static bool attr_done[kMaxDevices] = {};
+    static const int poly = [] {   // SH_ATTN_POLY = 0 / 2 / 3: exponentials per 8 keys computed on the FMA pipe
+        const char *e = getenv("SH_ATTN_POLY");
+        const int v = e ? atoi(e) : kDefaultPoly;
+        return v == 0 || v == 2 || v == 3 ? v : kDefaultPoly;
+    }();
+    auto kern = poly == 3 ? k_attn_tc<3> : poly == 2 ? k_attn_tc<2> : k_attn_tc<0>;
+    static bool attr_done[3][kMaxDevices] = {};
     const int dev = current_device() % kMaxDevices;
-    if (!attr_done[dev]) {
-        if (!cuda_ok(cudaFuncSetAttribute(k_attn_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kAttnSmem),
+    if (!attr_done[poly == 3 ? 2 : poly == 2 ? 1 : 0][dev]) {
+        if (!cuda_ok(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kAttnSmem),
                      "cudaFuncSetAttribute(attention)"))
             return -1;
-        attr_done[dev] = true;
+        attr_done[poly == 3 ? 2 : poly == 2 ? 1 : 0][dev] = true;
     }
     AttnArgs a;
     a.S = S;
@@ -594,7 +628,7 @@ int attention_tc_launch(const __half *q, const __half *k, const __half *v, __hal
     a.sl2 = scale * 1.4426950408889634f;
     a.err = state().dev_err;
     const uint32_t grid = (uint32_t)std::min<uint64_t>(items, (uint64_t)state().num_sms);
-    k_attn_tc<<<grid, kAttnThreads, kAttnSmem, stream()>>>(mq, mk, mv, mo, a);
+    kern<<<grid, kAttnThreads, kAttnSmem, stream()>>>(mq, mk, mv, mo, a);
     *launched = true;
     return cuda_ok(cudaGetLastError(), "sh_attention") ? 0 : -1;
 }
