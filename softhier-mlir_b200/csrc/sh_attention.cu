@@ -383,10 +383,19 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                 return true;
             };
             for (uint32_t it = blockIdx.x; ok && it < a.items; it += gridDim.x) {
-                if (!mbar_wait(&q_full[qs], qph, abort, a.err)) break;
                 const uint32_t aq = smem_u32(sm + kQOff + qs * 2 * kTileBytes);
                 for (uint32_t j = 0; j < a.nkb; ++j) {
-                    if (!mbar_wait(&k_full[st], kph, abort, a.err)) {
+                    // at an item boundary the previous item's last P V goes first: its softmax waits on it to finish
+                    // the item, while the new item's scores are not needed before that
+                    if (j == 0 && have_prev) {
+                        if (!issue_pv(prev_st, prev_ph, prev_g, prev_first)) {
+                            ok = false;
+                            break;
+                        }
+                        have_prev = false;
+                    }
+                    if ((j == 0 && !mbar_wait(&q_full[qs], qph, abort, a.err)) ||
+                        !mbar_wait(&k_full[st], kph, abort, a.err)) {
                         ok = false;
                         break;
                     }
