@@ -141,9 +141,10 @@ extern "C" {
 uint32_t sh_attention_l1_bytes_q(uint32_t S, uint32_t dh, uint32_t sq) {
     (void)S;
     (void)sq;
-    // the tensor-core kernel (dh = 64): two Q slots of two 128 x 64 tiles, three K/V stages of 128 keys, two
-    // 128 x 128 P tiles, barriers and alignment; the CUDA-core kernel: one staged block of 32 keys of K and V in fp32
-    return dh == 64 ? 4 * 128 * 64 * 2 + 3 * 2 * 128 * 64 * 2 + 2 * 128 * 128 * 2 + 256 + 1024
+    // the tensor-core kernel (dh = 64): two Q slots of two 128 x 64 tiles, four K/V stages of 128 keys, two
+    // 128 x 64 O staging tiles, barriers and alignment; the CUDA-core kernel: one staged block of 32 keys of K and V
+    // in fp32
+    return dh == 64 ? 4 * 128 * 64 * 2 + 4 * 2 * 128 * 64 * 2 + 2 * 128 * 64 * 2 + 256 + 1024
                     : 2 * kSimtKeys * (dh <= 128 ? dh : 128) * 4;
 }
 
@@ -210,32 +211,33 @@ int sh_cuda_attention_batched(uint64_t q, uint64_t k, uint64_t v, uint64_t o, ui
 // Tensor-core path (dh = 64): a persistent, warp-specialised flash-attention kernel.
 // Work item = (sequence b, head h, pair of 128-row query tiles); a CTA per SM walks the items. 320 threads:
 //   warp 0 (one thread)  : TMA loads: the item's two Q tiles into one of two Q slots, K / V blocks of 128 keys into
-//                          a 3-stage ring (separate `full` barriers for K and V, one `empty` barrier per stage);
+//                          a 4-stage ring (separate `full` barriers for K and V, one `empty` barrier per stage);
 //   warp 1 (one thread)  : tcgen05.mma issue. Per key block g: S_t = Q_t K^T (M=128, N=128, K=64) for both tiles t
 //                          into tensor memory as soon as each softmax holds its previous scores, then (one block
 //                          behind, so the next scores are ready when a softmax finishes) O_t (+)= P_t V (M=128, N=64,
-//                          K=128; P K-major from shared memory, V MN-major). (One issuer thread per tile measured
+//                          K=128; P from tensor memory, V MN-major from shared memory). (One issuer thread per tile measured
 //                          6 % slower at B = 512, S = 256.)
 //   warps 2..5 / 6..9    : softmax of tile 0 / 1, one query row per thread (warp w reads TMEM lanes 32 (w % 4) ..).
 //                          The 128 scores of a block are loaded into registers at once (S is free for the next block
 //                          right after), the running max m is only raised when a block's max exceeds it by more than
 //                          8 (log2 units; P <= 2^8 then, exact in fp16), in which case O (in tensor memory) is
-//                          rescaled before the next P V accumulates. P = 2^(s sl2 - m) goes to shared memory in the
-//                          128-byte-swizzled K-major layout (fp16); l sums P in fp32. At the end of an item O / l is
-//                          staged (swizzled) in the P buffer and leaves by a TMA store.
+//                          rescaled before the next P V accumulates. P = 2^(s sl2 - m) goes to tensor memory as fp16
+//                          pairs (tcgen05.st; no shared-memory traffic for P); l sums P in fp32. At the end of an item
+//                          O / l is staged (128-byte swizzle) in shared memory and leaves by a TMA store.
 // Q/K/V/O are addressed through 3-D tensor maps [sequence, row, column]: rows past the end of a sequence read as zero
-// and are not written; keys past the end are masked to -inf. Tensor memory: S_0, S_1 (128 columns each), O_0, O_1
-// (64 each) in a 512-column allocation. Shared memory: Q 2 x 32 KB, K/V 3 x 32 KB, P 2 x 32 KB.
+// and are not written; keys past the end are masked to -inf. Tensor memory (512 columns): S_0, S_1 (128 each), P_0, P_1
+// (64 each), O_0, O_1 (64 each). Shared memory: Q 2 x 32 KB, K/V 4 x 32 KB, O staging 2 x 16 KB.
 // ================================================================================================================
 namespace {
 
 constexpr int kTcRows = 128, kTcKeys = 128, kTcDh = 64;
-constexpr int kKvStages = 3;
-constexpr uint32_t kTileBytes = kTcRows * kTcDh * 2;          // 16 KB: one Q, K or V tile
-constexpr uint32_t kPBytes = kTcRows * kTcKeys * 2;           // 32 KB: P of one query tile, two 64-key halves
-constexpr uint32_t kQOff = 0, kKvOff = 4 * kTileBytes, kPOff = kKvOff + kKvStages * 2 * kTileBytes;
-constexpr uint32_t kBarOff = kPOff + 2 * kPBytes;
+constexpr int kKvStages = 4;
+constexpr uint32_t kTileBytes = kTcRows * kTcDh * 2;          // 16 KB: one Q, K or V tile, or one O staging tile
+constexpr uint32_t kQOff = 0, kKvOff = 4 * kTileBytes, kStgOff = kKvOff + kKvStages * 2 * kTileBytes;
+constexpr uint32_t kBarOff = kStgOff + 2 * kTileBytes;
 constexpr uint32_t kAttnSmem = kBarOff + 256 + 1024;
+// tensor memory columns: S_t (fp32 scores), P_t (fp16 pairs), O_t (fp32 output) of query tile t
+constexpr uint32_t kTmS = 0, kTmP = 2 * kTcKeys, kTmO = kTmP + kTcKeys;
 constexpr uint32_t kAttnTmemCols = 512;
 constexpr uint32_t kAttnThreads = 320;
 constexpr float kRescaleLog2 = 8.f;
@@ -358,7 +360,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             // ---------------- MMA issuer ----------------
             constexpr uint32_t idesc_s = umma_idesc_f16(kTcRows, kTcKeys, 0, 0);
             constexpr uint32_t idesc_o = umma_idesc_f16(kTcRows, kTcDh, 0, 1);
-            const uint32_t p_addr = smem_u32(sm + kPOff);
             uint32_t qs = 0, qph = 0, st = 0, kph = 0, g = 0;
             // the P V of the previous block: its stage, block counter and whether it opens an item
             bool have_prev = false, prev_first = false;
@@ -371,11 +372,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                 for (uint32_t t = 0; t < 2; ++t) {
                     if (!mbar_wait(&p_full[t], pg & 1u, abort, a.err)) return false;
                     tc_fence_after();
-                    const uint32_t ap = p_addr + t * kPBytes;
+                    // P_t (128 x 128 keys) from tensor memory: 16 keys = 8 columns per MMA
 #pragma unroll
                     for (int k = 0; k < kTcKeys / 16; ++k)
-                        umma_f16_ss(tmem + 256 + t * kTcDh,
-                                    sw128_desc(ap + (k >> 2) * (kTcRows * 128) + (k & 3) * 32, 16, 1024),
+                        umma_f16_ts(tmem + kTmO + t * kTcDh, tmem + kTmP + t * (kTcKeys / 2) + k * 8,
                                     sw128_desc(av + k * 2048, 16384, 1024), idesc_o, (first && k == 0) ? 0u : 1u);
                     umma_commit(&o_full[t]);
                 }
@@ -410,7 +410,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                         tc_fence_after();
 #pragma unroll
                         for (int k = 0; k < kTcDh / 16; ++k)
-                            umma_f16_ss(tmem + t * kTcKeys, sw128_desc(aq + t * kTileBytes + k * 32, 16, 1024),
+                            umma_f16_ss(tmem + kTmS + t * kTcKeys, sw128_desc(aq + t * kTileBytes + k * 32, 16, 1024),
                                         sw128_desc(ak + k * 32, 16, 1024), idesc_s, k > 0 ? 1u : 0u);
                         umma_commit(&s_full[t]);
                     }
@@ -447,9 +447,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const uint32_t quarter = warp & 3u;
         const uint32_t r = quarter * 32 + lane;                  // query row within the tile
         const uint32_t lane_base = tmem + ((quarter * 32u) << 16);
-        const uint32_t s_addr = lane_base + t * kTcKeys, o_addr = lane_base + 256 + t * kTcDh;
-        uint8_t *pt = sm + kPOff + t * kPBytes;
-        uint8_t *prow = pt + r * 128;
+        const uint32_t s_addr = lane_base + kTmS + t * kTcKeys, p_addr = lane_base + kTmP + t * (kTcKeys / 2);
+        const uint32_t o_addr = lane_base + kTmO + t * kTcDh;
+        uint8_t *stg = sm + kStgOff + t * kTileBytes;     // O staging of tile t: 128 rows x 128 B, 128-byte swizzle
+        uint8_t *srow = stg + r * 128;
         uint32_t g = 0;
         bool store_pending = false, ok = true;
         for (uint32_t it = blockIdx.x; ok && it < a.items; it += gridDim.x) {
@@ -509,28 +510,24 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                     l *= alpha;
                     m = mb;
                 }
-                if (store_pending) {
-                    if (lane == 0) bulk_wait_read0();
-                    __syncwarp();
-                    store_pending = false;
-                }
+                // P = 2^(s sl2 - m) as fp16 pairs into tensor memory (64 columns per row), in four parts of 32 keys
                 float ls8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-                for (int u = 0; u < kTcKeys / 8; ++u) {
-                    uint32_t packed[4];
+                for (int h = 0; h < 4; ++h) {
+                    uint32_t packed[16];
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const float x0 = fmaf(sc[8 * u + 2 * i], a.sl2, -m);
-                        const float x1 = fmaf(sc[8 * u + 2 * i + 1], a.sl2, -m);
-                        const float p0 = (2 * i < POLY) ? exp2_poly(x0) : fast_exp2(x0);
-                        const float p1 = (2 * i + 1 < POLY) ? exp2_poly(x1) : fast_exp2(x1);
-                        ls8[2 * i] += p0;
-                        ls8[2 * i + 1] += p1;
+                    for (int i = 0; i < 16; ++i) {
+                        const int k0 = 32 * h + 2 * i;
+                        const float x0 = fmaf(sc[k0], a.sl2, -m);
+                        const float x1 = fmaf(sc[k0 + 1], a.sl2, -m);
+                        const float p0 = ((2 * i) % 8 < POLY) ? exp2_poly(x0) : fast_exp2(x0);
+                        const float p1 = ((2 * i + 1) % 8 < POLY) ? exp2_poly(x1) : fast_exp2(x1);
+                        ls8[(2 * i) & 7] += p0;
+                        ls8[(2 * i + 1) & 7] += p1;
                         const __half2 hp = __floats2half2_rn(p0, p1);
                         packed[i] = *reinterpret_cast<const uint32_t *>(&hp);
                     }
-                    *reinterpret_cast<uint4 *>(prow + (u >> 3) * (kTcRows * 128) + (((u & 7u) ^ (r & 7u)) * 16)) =
-                        make_uint4(packed[0], packed[1], packed[2], packed[3]);
+                    tmem_st_32x32b_x16(p_addr + 16 * h, packed);
                 }
                 l += ((ls8[0] + ls8[1]) + (ls8[2] + ls8[3])) + ((ls8[4] + ls8[5]) + (ls8[6] + ls8[7]));
                 if (__any_sync(0xffffffffu, raise)) {   // O *= alpha before the next P V accumulates into it
@@ -544,17 +541,20 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                         for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
                         tmem_st_32x32b_x32(o_addr + c * 32, v);
                     }
-                    tmem_st_wait();
                 }
-                fence_proxy_async_smem();
+                tmem_st_wait();   // P (and a rescaled O) in tensor memory before the MMA may read it
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&p_full[t]);
             }
             if (!ok) break;
-            // ---- item epilogue: O / l -> fp16, staged in this warp's 32 rows of P's first half, one TMA store ----
+            // ---- item epilogue: O / l -> fp16, staged in this warp's 32 rows of the staging tile, one TMA store ----
             if (!mbar_wait(&o_full[t], (g - 1u) & 1u, abort, a.err)) break;
             tc_fence_after();
+            if (store_pending) {   // the previous item's O is still being read out of the staging rows
+                if (lane == 0) bulk_wait_read0();
+                __syncwarp();
+            }
             const float inv = 1.f / l;
 #pragma unroll
             for (int c = 0; c < kTcDh / 32; ++c) {
@@ -570,7 +570,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                         hh[i] = __floats2half2_rn(__uint_as_float(v[8 * q + 2 * i]) * inv,
                                                   __uint_as_float(v[8 * q + 2 * i + 1]) * inv);
                     const uint32_t u = c * 4 + q;
-                    *reinterpret_cast<uint4 *>(prow + ((u ^ (r & 7u)) * 16)) = out;
+                    *reinterpret_cast<uint4 *>(srow + ((u ^ (r & 7u)) * 16)) = out;
                 }
             }
             tc_fence_before();
@@ -578,7 +578,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             __syncwarp();
             if (lane == 0) {
                 const uint32_t qp = it % a.nqp, bh = it / a.nqp;
-                tma_store_3d(&mo, pt + quarter * 32 * 128, (int32_t)((bh % a.H) * kTcDh),
+                tma_store_3d(&mo, stg + quarter * 32 * 128, (int32_t)((bh % a.H) * kTcDh),
                              (int32_t)(qp * 2 * kTcRows + t * kTcRows + quarter * 32), (int32_t)(bh / a.H));
                 bulk_commit();
             }
