@@ -28,6 +28,7 @@ namespace {
 constexpr int BM = 128;
 constexpr int BK = 64;
 constexpr int kThreads = 320;   // warp 0 TMA, warp 1 MMA, warps 2..9 epilogue
+constexpr int kPairThreads = 352;   // the 2-CTA kernel adds warp 10: forwards the epilogue's "accumulator drained"
 constexpr uint32_t kEpiWarps = 8;
 
 constexpr uint32_t kEpiStageBytes = 8 * 4096;   // per epilogue warp: two 32 x 32 fp16 store tiles
@@ -488,8 +489,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 // both CTAs' TMA transactions complete on the leader's `full` barrier, the leader's single thread issues
 // tcgen05.mma.cta_group::2 (M = 256), and its commits arrive on the `empty` / `tfull` barriers of both CTAs. Each
 // CTA's tensor memory holds its own 128 rows of the accumulator (all BN columns), which its 8 epilogue warps drain
-// exactly like the single-CTA kernel before arriving on the leader's `tempty` barrier (16 arrivals). Per stage and
-// SM, W traffic is half that of the single-CTA tile. No split-K (the caller picks this kernel only without it).
+// exactly like the single-CTA kernel; they arrive on a local barrier, and warp 10 of each CTA forwards one arrive to
+// the leader's `tempty` barrier (2 arrivals). Per stage and SM, W traffic is half that of the single-CTA tile. No
+// split-K (the caller picks this kernel only without it).
 constexpr int kPairStages = 6;
 
 template <int BN>
@@ -502,7 +504,7 @@ struct PairCfg {
 };
 
 template <int BN>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     k_gemm_tc2(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w,
                const __grid_constant__ CUtensorMap map_z, GemmArgs a) {
     using C = PairCfg<BN>;
@@ -516,7 +518,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     uint64_t *tfull = empty + S;
     uint64_t *tempty = tfull + 2;
     uint64_t *mdone = tempty + 2;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mdone + 1);
+    uint64_t *epi_done = mdone + 1;   // [2] this CTA's 8 epilogue warps have drained accumulator buffer i
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(epi_done + 2);
     volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -529,8 +532,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             mbar_init(&empty[s], 1);    // both: the leader's commit
         }
         for (int i = 0; i < 2; ++i) {
-            mbar_init(&tfull[i], 1);                 // both: the leader's commit
-            mbar_init(&tempty[i], 2 * kEpiWarps);    // leader: every epilogue warp of both CTAs
+            mbar_init(&tfull[i], 1);         // both: the leader's commit
+            mbar_init(&tempty[i], 2);        // leader: warp 10 of both CTAs
+            mbar_init(&epi_done[i], kEpiWarps);
         }
         mbar_init(mdone, 1);
         *abort = 0;
@@ -616,13 +620,27 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             umma_commit_pair_both(mdone);   // both CTAs: every MMA the leader issued has completed
         }
         if (lane == 0) drain_wait(mdone, 0);
+    } else if (warp == 10) {
+        // A remote mbarrier arrive (release, cluster scope) stalls its thread for ~2000 cycles; this warp takes
+        // that stall instead of the epilogue warps: it waits for the local epilogue_done barrier of the buffer and
+        // forwards one arrive to the leader's tempty barrier.
+        if (lane == 0) {
+            const uint32_t tempty_leader[2] = {mapa_shared(smem_u32(&tempty[0]), 0),
+                                               mapa_shared(smem_u32(&tempty[1]), 0)};
+            uint32_t acc = 0, acc_phase = 0;
+            for (uint32_t u = pair; u < total_units; u += npairs) {
+                if (!mbar_wait(&epi_done[acc], acc_phase, abort, a.err)) break;
+                mbar_arrive_cluster(tempty_leader[acc]);
+                acc ^= 1u;
+                if (acc == 0) acc_phase ^= 1u;
+            }
+        }
     } else {
         const uint32_t quarter = warp & 3u;
         const uint32_t half = (warp - 2u) >> 2;
         constexpr uint32_t HB = BN / 2;
         const uint32_t row_in_tile = rank * 128 + quarter * 32 + lane;
         const bool want_res = (a.flags & SH_EPI_RESIDUAL) != 0;
-        const uint32_t tempty_leader[2] = {mapa_shared(smem_u32(&tempty[0]), 0), mapa_shared(smem_u32(&tempty[1]), 0)};
         uint8_t *stg = epi_stage + (warp - 2u) * 4096u;
         uint32_t nst = 0;
         if (a.tma_store && lane == 0) prefetch_tmap(&map_z);
@@ -657,7 +675,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive_cluster(tempty_leader[acc]);
+            if (lane == 0) mbar_arrive(&epi_done[acc]);
             acc ^= 1u;
             if (acc == 0) acc_phase ^= 1u;
         }
@@ -797,7 +815,7 @@ int launch_pair(const Plan &p, const CUtensorMap &mx, const CUtensorMap &mw, con
     a.num_tiles = ((a.M + 255) / 256) * p.tiles_n;
     a.splits = 1;
     const uint32_t pairs = min(a.num_tiles, (uint32_t)sh::state().num_sms / 2);
-    k_gemm_tc2<BN><<<2 * pairs, kThreads, PairCfg<BN>::kSmem, st>>>(mx, mw, mz, a);
+    k_gemm_tc2<BN><<<2 * pairs, kPairThreads, PairCfg<BN>::kSmem, st>>>(mx, mw, mz, a);
     return sh::cuda_ok(cudaGetLastError(), "sh_gemm launch (pair)") ? 0 : -1;
 }
 
