@@ -407,8 +407,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!mbar_wait(&tfull[acc], acc_phase, abort, a.err)) break;
             tc_fence_after();
             const uint32_t taddr = tmem_base + ((quarter * 32u) << 16) + acc * BN + half * HB;
+            // partial tile of this split: warp-interleaved so that every store (and the reducer's load) of a warp
+            // covers 512 contiguous bytes: value 4 q + j of chunk c of epilogue warp e, lane l, lives at float
+            // ((e * HB / 32 + c) * 8 + q) * 128 + 4 l + j of the tile-split block
             float *part = a.splits > 1 ? a.ws + ((size_t)tile * a.splits + split) * (BM * BN) +
-                                             (size_t)row_in_tile * BN + half * HB
+                                             (size_t)(warp - 2u) * (HB / 32) * 1024 + lane * 4
                                        : nullptr;
 #pragma unroll 1
             for (uint32_t c = 0; c < HB / 32; ++c) {
@@ -418,7 +421,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (part) {
 #pragma unroll
                     for (int i = 0; i < 8; ++i)
-                        reinterpret_cast<float4 *>(part + c * 32)[i] =
+                        *reinterpret_cast<float4 *>(part + c * 1024 + i * 128) =
                             make_float4(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]),
                                         __uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3]));
                     continue;
@@ -442,30 +445,46 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (acc == 0) acc_phase ^= 1u;
 
             if (a.splits > 1) {
-                // arrival counter: the last split of this tile reduces the partials in split order
-                __threadfence();
+                // arrival counter: the last split of this tile reduces the partials in split order. The epilogue
+                // warps' partial stores are ordered before one thread's acquire-release atomic by the CTA barrier
+                // (release is cumulative), and the last CTA's loads after it by the second barrier; a fence by every
+                // thread is not needed.
                 if (!epi_sync(esync, es_phase, abort, a.err)) break;
                 if (threadIdx.x == 64) {
-                    const uint32_t t = atomicAdd(&a.counters[tile], 1u);
+                    const uint32_t t = atom_add_acq_rel_gpu(&a.counters[tile], 1u);
                     const uint32_t last = (t == a.splits - 1) ? 1u : 0u;
                     if (last) a.counters[tile] = 0;   // ready for the next launch (stream order)
                     *last_flag = last;
                 }
                 if (!epi_sync(esync, es_phase, abort, a.err)) break;
                 if (*last_flag) {
-                    __threadfence();
+                    // sum the partial tiles in split order, 32 columns at a time with a whole split's row segment
+                    // (8 x 16 B) in flight per load batch, then the same fused epilogue as an unsplit tile
                     const float *base =
-                        a.ws + (size_t)tile * a.splits * (BM * BN) + (size_t)row_in_tile * BN + half * HB;
+                        a.ws + (size_t)tile * a.splits * (BM * BN) + (size_t)(warp - 2u) * (HB / 32) * 1024 + lane * 4;
 #pragma unroll 1
-                    for (uint32_t c = 0; c < HB / 8; ++c) {
-                        float v[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-                        for (uint32_t s = 0; s < a.splits; ++s) {
-                            const float4 *p = reinterpret_cast<const float4 *>(base + (size_t)s * (BM * BN) + c * 8);
-                            const float4 p0 = __ldcg(p), p1 = __ldcg(p + 1);
-                            v[0] += p0.x; v[1] += p0.y; v[2] += p0.z; v[3] += p0.w;
-                            v[4] += p1.x; v[5] += p1.y; v[6] += p1.z; v[7] += p1.w;
+                    for (uint32_t c = 0; c < HB / 32; ++c) {
+                        float v[32];
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) v[i] = 0.f;
+#pragma unroll 2
+                        for (uint32_t sp = 0; sp < a.splits; ++sp) {
+                            const float *p = base + (size_t)sp * (BM * BN) + c * 1024;
+                            float4 q[8];
+#pragma unroll
+                            for (int i = 0; i < 8; ++i) q[i] = __ldcg(reinterpret_cast<const float4 *>(p + i * 128));
+#pragma unroll
+                            for (int i = 0; i < 8; ++i) {
+                                v[4 * i] += q[i].x;
+                                v[4 * i + 1] += q[i].y;
+                                v[4 * i + 2] += q[i].z;
+                                v[4 * i + 3] += q[i].w;
+                            }
                         }
-                        epilogue8(a, row, col0 + c * 8, v);
+                        const uint32_t col = col0 + c * 32;
+                        uint4 res[4] = {};
+                        if (res_vec && col + 32 <= a.N) load32(a.resid + (size_t)row * a.ldr + col, res);
+                        epi_chunk(a, &map_z, stg, nst, row, row_base, col, v, res, lane);
                     }
                 }
                 // last_flag is rewritten for the next tile only after every warp has read it
@@ -768,9 +787,11 @@ Plan make_plan(uint32_t M, uint32_t N, uint32_t K, uint32_t splits_req, int num_
     const uint32_t tiles = p.tiles_m * p.tiles_n;
     uint32_t s = 1;
     if (splits_req == 0) {
-        if (tiles * 2 <= (uint32_t)num_sms && p.k_blocks >= 8) {
+        // a split costs ~1.3 us of partial-tile traffic and reduction: only K loops of 16+ blocks are split, into
+        // pieces of at least 8 blocks (512^3: unsplit 5.7 us, 2 splits 6.9; 256 x 768 x 3072: unsplit 17.0, 6 splits 9.4)
+        if (tiles * 2 <= (uint32_t)num_sms && p.k_blocks >= 16) {
             s = (uint32_t)num_sms / tiles;
-            s = min(s, p.k_blocks / 4);   // at least 4 K-blocks per split
+            s = min(s, p.k_blocks / 8);
             s = min(s, 16u);
             s = max(s, 1u);
         }

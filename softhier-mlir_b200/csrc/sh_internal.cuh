@@ -130,6 +130,13 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volati
     }
 }
 
+// atomic add with acquire-release semantics at GPU scope; returns the old value
+__device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t *p, uint32_t v) {
+    uint32_t old;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+
 // Bounded wait that ignores the abort flag: used to drain outstanding asynchronous work before exit.
 __device__ __forceinline__ void drain_wait(uint64_t *bar, uint32_t parity) {
     const long long t0 = clock64();
