@@ -15,7 +15,8 @@ dimensions / element offsets, 263-270 the gemm cfg, 280-605 op -> call, 608-669 
   - `cluster` = -1 -> SH_ALL, -2 -> SH_SELF, absent -> 0;
   - prologue = test fills and the preload wait, epilogue = whole-buffer checks and the sample dumps of buffers no
     later op touches, kernel = the rest.
-The module-level passes linalg-to-softhier / distribute-summa / pipeline-gemm are applied when requested.
+The module-level passes linalg-to-softhier / distribute-summa / pipeline-gemm are applied when requested, and
+`fuse-epilogues` (this backend's own) folds add_bias / gelu / residual add into the producing GEMM.
 """
 from __future__ import annotations
 
@@ -59,9 +60,89 @@ def apply_passes(fn: D.Func, passes: list[str] | tuple[str, ...] = ()) -> D.Func
             fn = D.mark_gemms(fn, "summa")
         elif p == "pipeline-gemm":
             fn = D.mark_gemms(fn, "pipeline")
+        elif p == "fuse-epilogues":
+            fn = fuse_epilogues(fn)
         else:
             raise ValueError(f"unknown pass {p}")
     return fn
+
+
+# ---- epilogue fusion (this backend only) ------------------------------------------------------------------------------
+FUSED = "softhier.gemm_fused"     # internal op: operands [x, w, bias(, residual)], into [z]; attrs["epi"] flags
+
+
+def _tiles_ok(op: D.Op, m: int, n: int, k: int) -> bool:
+    """sh_gemm's own shape checks (sh_gemm.inc.c:60-68) pass, so fusing cannot hide a -1 / -3 the module would see."""
+    a = op.attrs
+    tm, tn, tk = (int(a.get(t, 0)) or 256 for t in ("tile_m", "tile_n", "tile_k"))
+    return a.get("fmt", "fp16") == "fp16" and m % tm == 0 and n % tn == 0 and k % tk == 0
+
+
+def _read_before_overwrite(z: str, later: list[D.Op], defs: dict[str, D.Op]) -> bool:
+    """Whether a later op may read buffer z (or a view of its buffer) before a plain GEMM overwrites all of z."""
+    zbase = _base(z, defs)
+    for lo in later:
+        mentioned = [v for v in _all_operands(lo) if _base(v, defs) == zbase]
+        if not mentioned:
+            continue
+        return not (lo.name == "softhier.gemm" and not lo.body and "accumulate" not in lo.attrs
+                    and lo.into == [z] and defs[z].name == "softhier.hbm_buffer"
+                    and all(_base(v, defs) != zbase for v in lo.operands))
+    return False
+
+
+def _fuse_list(ops: list[D.Op], defs: dict[str, D.Op]) -> list[D.Op]:
+    out: list[D.Op] = []
+    i = 0
+    while i < len(ops):
+        op = ops[i]
+        if op.body:
+            op = D.Op(name=op.name, results=op.results, operands=op.operands, into=op.into, outs=op.outs,
+                      attrs=op.attrs, types=op.types, result_type=op.result_type, body=_fuse_list(op.body, defs),
+                      text=op.text)
+        nxt = ops[i + 1] if i + 1 < len(ops) else None
+        if (op.name == "softhier.gemm" and not any(t in op.attrs for t in ("summa", "xmcast", "accumulate"))
+                and nxt is not None and nxt.name == "softhier.add_bias" and nxt.operands[0] == op.into[0]
+                and nxt.outs == op.into):
+            x, w, z = op.operands[0], op.operands[1], op.into[0]
+            mx, mw, mz = (defs[v].result_type for v in (x, w, z))
+            m, k = mx.geom()[:2]
+            n = mw.geom()[1]
+            if _tiles_ok(op, m, n, k) and mz.geom()[:2] == (m, n):
+                bias = nxt.operands[1]
+                flags, dst, resid, used = L.EPI_BIAS, z, None, 2
+                third = ops[i + 2] if i + 2 < len(ops) else None
+                z_read_later = _read_before_overwrite(z, ops[i + 3:], defs)
+                if third is not None and not z_read_later:
+                    if (third.name == "softhier.gelu" and third.operands[0] == z
+                            and defs[third.outs[0]].result_type.geom()[:2] == (m, n)):
+                        flags, dst, used = flags | L.EPI_GELU, third.outs[0], 3
+                    elif (third.name == "softhier.add" and "train" not in third.attrs and z in third.operands[:2]
+                          and third.operands[0] != third.operands[1]
+                          and defs[third.outs[0]].result_type.geom()[:2] == (m, n)):
+                        r = third.operands[1] if third.operands[0] == z else third.operands[0]
+                        if defs[r].result_type.geom()[:2] == (m, n):
+                            flags, dst, resid, used = flags | L.EPI_RESIDUAL, third.outs[0], r, 3
+                fused = D.Op(name=FUSED, operands=[x, w, bias] + ([resid] if resid else []), into=[dst],
+                             attrs={"epi": flags, "tile_m": op.attrs.get("tile_m", 0),
+                                    "tile_n": op.attrs.get("tile_n", 0), "tile_k": op.attrs.get("tile_k", 0)},
+                             types=op.types, text=f"{FUSED} (from: {op.text.strip()[:60]} ...)")
+                out.append(fused)
+                i += used
+                continue
+        out.append(op)
+        i += 1
+    return out
+
+
+def fuse_epilogues(fn: D.Func) -> D.Func:
+    """`fuse-epilogues`: a plain fp16 softhier.gemm X, W into Z followed by `add_bias Z, b -> Z` becomes one GEMM
+    with the bias in its epilogue; when the next op is `gelu Z -> G` or `add Z, R -> H` (either operand order) and
+    nothing later reads Z, that op joins too (bias + tanh-GELU into G, or bias + residual R into H). The frontend's
+    SigLIP layer (frontend/siglip.py:136-166) goes from 16 calls to 9. Results differ from the unfused program only by
+    rounding: the fused epilogue rounds once to fp16 instead of after every op."""
+    defs = _defs(fn.ops)
+    return D.Func(name=fn.name, ops=_fuse_list(fn.ops, defs))
 
 
 # ---- values: buffers and index expressions --------------------------------------------------------------------------
@@ -216,6 +297,21 @@ def _emit_ops(ops: list[D.Op], sc: Scope, defs: dict, out: list[str], tag: str, 
             else:
                 out.append(f"{ind}{{ sh_gemm_cfg cfg = {_gemm_cfg_c(op)};")
                 out.append(f"{ind}  sh_gemm({args}, {_cluster_c(a)}); }}")
+        elif n == FUSED:
+            x, w, b = op.operands[:3]
+            z = op.into[0]
+            m, k, ldx, _ = sc.bufs[x].mt.geom()
+            _, nn, ldw, _ = sc.bufs[w].mt.geom()
+            ldz = sc.bufs[z].mt.geom()[2]
+            if len(op.operands) > 3:
+                r = op.operands[3]
+                res, ldr = sc.haddr(r), sc.bufs[r].mt.geom()[2]
+            else:
+                res, ldr = "0", ldz
+            epi = [f for f, bit in (("SH_EPI_BIAS", L.EPI_BIAS), ("SH_EPI_GELU", L.EPI_GELU),
+                                    ("SH_EPI_RESIDUAL", L.EPI_RESIDUAL)) if op.attrs["epi"] & bit]
+            out.append(f"{ind}sh_cuda_gemm({sc.haddr(x)}, {sc.haddr(w)}, {sc.haddr(z)}, {m}, {nn}, {k}, {ldx}, {ldw}, "
+                       f"{ldz}, {sc.haddr(b)}, {res}, {ldr}, {' | '.join(epi)}, 0);  // fused epilogue")
         elif n == "softhier.hbm_fill":
             rows, cols = op.types[0].shape[:2] if len(op.types[0].shape) > 1 else (1, op.types[0].shape[0])
             out.append(f"{ind}sh_test_fill_const_fp16({sc.bufs[op.operands[0]].name}, {rows}, {cols}, {cols}, "
@@ -319,6 +415,7 @@ def emit_kernel(fn: D.Func, phase: str | None = None) -> str:
 _MAIN = """\
 // Generated by softhier_cuda.emit_cuda (softhier dialect -> libsh_ops_cuda.so calls). Do not edit by hand.
 #include "sh_ops.h"
+#include "sh_ops_cuda.h"
 
 static void {k}_inputs(void) {{   // preload wait + test inputs (not timed)
 {pro}
@@ -431,6 +528,12 @@ class Program:
                 mode = {"auto": 0, "panel": 1, "whole": 2}[a["xmcast"] if isinstance(a["xmcast"], str) else "auto"]
                 return lib.sh_gemm_xmcast_ex(*args, mode)
             return lib.sh_gemm(*args, _cluster_v(a))
+        if n == FUSED:
+            (x, mx), (w, mw), (b, _), (z, mz) = A(op.operands[0]), A(op.operands[1]), A(op.operands[2]), A(op.into[0])
+            m, k, ldx, _ = mx.geom()
+            _, nn, ldw, _ = mw.geom()
+            r, ldr = (A(op.operands[3])[0], A(op.operands[3])[1].geom()[2]) if len(op.operands) > 3 else (0, mz.geom()[2])
+            return lib.sh_cuda_gemm(x, w, z, m, nn, k, ldx, ldw, mz.geom()[2], b, r, ldr, op.attrs["epi"], 0)
         if n == "softhier.layernorm":
             (x, mx), (g, _), (b, _), (y, _) = A(op.operands[0]), A(op.operands[1]), A(op.operands[2]), A(op.outs[0])
             rows, cols, ld, _ = mx.geom()

@@ -88,14 +88,39 @@ def test_siglip_frontend_module_fused_two_layers():
     assert "sh_attention_q(hb3, hb4, hb5, hb6, 64, 128, 2, 128, 128, 128, 128, 0.125f, SH_ALL, 64);" in c
 
 
+def test_fuse_epilogues_pass():
+    """fuse-epilogues: gemm + add_bias (+ gelu | + residual add) -> one sh_cuda_gemm; the SigLIP layer goes from 16
+    calls to 9; buffers that later ops read before a GEMM overwrites them are left unfused."""
+    c = E.emit_c((MLIR / "siglip_s256_fused.mlir").read_text(), ("fuse-epilogues",))
+    k = _calls(c)
+    assert k == {"sh_cuda_gemm": 6, "sh_layernorm": 2, "sh_attention_q": 1, "sh_barrier_global": 1,
+                 "sh_hbm_addr": k["sh_hbm_addr"], "sh_cluster_id": 4, "sh_is_first_core": 4, "sh_printf": 4,
+                 "sh_cycles": 4}
+    assert "sh_cuda_gemm(hb2, hb14, hb3, 256, 768, 768, 768, 768, 768, hb20, 0, 768, SH_EPI_BIAS, 0);" in c
+    # o projection: h = x + (o wo + bo); FC1: g = gelu(ln2 w1 + b1); FC2: out = h + (g w2 + b2)
+    assert "sh_cuda_gemm(hb6, hb17, hb8, 256, 768, 768, 768, 768, 768, hb23, hb1, 768, SH_EPI_BIAS | SH_EPI_RESIDUAL, 0);" in c
+    assert "sh_cuda_gemm(hb9, hb18, hb11, 256, 3072, 768, 768, 3072, 3072, hb24, 0, 3072, SH_EPI_BIAS | SH_EPI_GELU, 0);" in c
+    assert "sh_cuda_gemm(hb11, hb19, hb13, 256, 768, 3072, 3072, 768, 768, hb25, hb8, 768, SH_EPI_BIAS | SH_EPI_RESIDUAL, 0);" in c
+    # two stacked layers: the second layer's GEMMs overwrite ao / f1 / f2 before reading them, so both layers fuse
+    k2 = _calls(E.emit_c((MLIR / "siglip_s64_fused_l2.mlir").read_text(), ("fuse-epilogues",)))
+    assert k2["sh_cuda_gemm"] == 12 and "sh_add" not in k2 and "sh_gelu" not in k2 and "sh_add_bias" not in k2
+    # a dump of the pre-GELU buffer keeps the GELU separate (bias still fuses in place)
+    t = (MLIR / "siglip_s256_fused.mlir").read_text()
+    dump = ('    softhier.dump_samples %f1 {tag = "F1", seed = 5 : i32, n = 8 : i32} : '
+            'memref<256x3072xf16, "hbm_west">\n    func.return')
+    k3 = _calls(E.emit_c(t.replace("    func.return", dump, 1), ("fuse-epilogues",)))
+    assert k3["sh_gelu"] == 1 and k3["sh_cuda_gemm"] == 6
+
+
 @pytest.mark.skipif(shutil.which("gcc") is None, reason="no C compiler")
-def test_emitted_program_compiles_and_links(tmp_path):
-    """The generated main.c builds against include/sh_ops.h and links with libsh_ops_cuda.so (no run)."""
+@pytest.mark.parametrize("passes", [(), ("fuse-epilogues",)])
+def test_emitted_program_compiles_and_links(tmp_path, passes):
+    """The generated main.c builds against include/ and links with libsh_ops_cuda.so (no run)."""
     lib = ROOT / "softhier-mlir_b200" / "lib"
     if not (lib / "libsh_ops_cuda.so").exists():
         pytest.skip("library not built")
     src = tmp_path / "main.c"
-    src.write_text(E.emit_c((MLIR / "siglip_s256_perhead.mlir").read_text()))
+    src.write_text(E.emit_c((MLIR / "siglip_s256_perhead.mlir").read_text(), passes))
     r = subprocess.run(["gcc", "-O1", "-Wall", "-Wno-unused-variable", "-Werror", "-I", str(ROOT / "include"), str(src), "-L", str(lib),
                         "-lsh_ops_cuda", "-o", str(tmp_path / "main")], capture_output=True, text=True)
     assert r.returncode == 0, r.stderr

@@ -28,11 +28,13 @@ def _run(rt, text, capfd, passes=()):
     return prog, capfd.readouterr().out
 
 
+@pytest.mark.parametrize("passes", [(), ("fuse-epilogues",)])
 @pytest.mark.parametrize("name", ["siglip_s256_perhead.mlir", "siglip_s256_fused.mlir"])
-def test_siglip_layer_module_matches_reference(gpu_lib, capfd, name):
+def test_siglip_layer_module_matches_reference(gpu_lib, capfd, name, passes):
     """Config 3 lowered from frontend/siglip.py: sampled dumps within the reference's 0.05 / 0.05 (run.py:360-365)
-    against siglip_ref's own values, and every full tensor against the oracle."""
-    prog, out = _run(gpu_lib, (MLIR / name).read_text(), capfd)
+    against siglip_ref's own values, and every full tensor against the oracle; unfused and with the GEMM epilogues
+    fused."""
+    prog, out = _run(gpu_lib, (MLIR / name).read_text(), capfd, passes)
     got = lcg.parse_samples(out)
     g = golden("siglip_s256.npz")
     tags = [t for t in TAGS if t in got]
@@ -54,9 +56,10 @@ def test_siglip_layer_module_matches_reference(gpu_lib, capfd, name):
         assert np.all(err <= 0.05 + 0.05 * np.abs(ref[tag])), (tag, float(err.max()))
 
 
-def test_two_layer_fused_module(gpu_lib, capfd):
+@pytest.mark.parametrize("passes", [(), ("fuse-epilogues",)])
+def test_two_layer_fused_module(gpu_lib, capfd, passes):
     """Two stacked layers (frontend seeds 100 * layer), small shape with explicit 64^3 GEMM tiles."""
-    prog, out = _run(gpu_lib, (MLIR / "siglip_s64_fused_l2.mlir").read_text(), capfd)
+    prog, out = _run(gpu_lib, (MLIR / "siglip_s64_fused_l2.mlir").read_text(), capfd, passes)
     x, p0 = siglip.lcg_layer_inputs(64, 128, 256, 0)
     _, p1 = siglip.lcg_layer_inputs(64, 128, 256, 1)
     want = siglip.encoder_reference(x, [p0, p1], 2, scale=0.125)
