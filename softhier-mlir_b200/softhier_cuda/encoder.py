@@ -140,16 +140,17 @@ def layer_forward(lib, act: Activations, w: LayerWeights, heads: int, eps: float
 
 
 def encoder_schedule(lib, act: Activations, layers: list[LayerWeights], heads: int, eps: float, scale: float,
-                     x_in: int | None = None) -> tuple[list[tuple[str, Callable[[], int]]], int]:
+                     x_in: int | None = None, x_out: int | None = None) -> tuple[list[tuple[str, Callable[[], int]]], int]:
     """Every call of a full forward pass and the address the result lands in. Layer 0 reads x_in (default act.x),
     later layers ping-pong the residual stream between act.out and act.x, so x_in is never overwritten when it is a
-    separate buffer."""
+    separate buffer; x_out, when given, receives the last layer's output instead of the ping-pong buffer."""
     cur = act.x if x_in is None else x_in
     nxt = act.out
     sched = []
     for i, w in enumerate(layers):
-        sched += layer_ops(lib, act, w, heads, eps, scale, cur, nxt)
-        cur, nxt = nxt, (act.x if nxt == act.out else act.out)
+        dst = x_out if (x_out is not None and i == len(layers) - 1) else nxt
+        sched += layer_ops(lib, act, w, heads, eps, scale, cur, dst)
+        cur, nxt = dst, (act.x if nxt == act.out else act.out)
     return sched, cur
 
 
