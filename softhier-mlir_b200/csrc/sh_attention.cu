@@ -241,20 +241,6 @@ constexpr uint32_t kTmS = 0, kTmP = 2 * kTcKeys, kTmO = kTmP + kTcKeys;
 constexpr uint32_t kAttnTmemCols = 512;
 constexpr uint32_t kAttnThreads = 320;
 constexpr float kRescaleLog2 = 8.f;
-constexpr int kDefaultPoly = 0;
-
-// 2^x on the FMA pipe, for x <= 16 (a share of the softmax exponentials is computed here instead of on the special
-// function unit, which otherwise bounds the softmax): x = n + f with n = round(x) (by the 1.5 * 2^23 addition trick)
-// and f in [-0.5, 0.5]; 2^f by a cubic whose coefficients were fit for minimal relative error on [-0.5, 0.5] by
-// Lawson-weighted least squares (max relative error 7.5e-5, below half an fp16 ulp); 2^n is added to the exponent
-// field. x is clamped at -126 so that the result stays a (sub)normal positive number; P rounds to fp16 zero there.
-__device__ __forceinline__ float exp2_poly(float x) {
-    x = fmaxf(x, -126.f);
-    const float t = x + 12582912.f;
-    const float f = x - (t - 12582912.f);
-    const float p = fmaf(fmaf(fmaf(0.0551716685f, f, 0.2426111400f), f, 0.6932609677f), f, 0.9999280572f);
-    return __int_as_float(__float_as_int(p) + ((__float_as_int(t) - 0x4B400000) << 23));
-}
 
 struct AttnArgs {
     uint32_t S, H, nkb, nqp, items;
@@ -262,8 +248,6 @@ struct AttnArgs {
     int *err;
 };
 
-// POLY of every 8 consecutive keys take exp2_poly, the rest the special function unit
-template <int POLY>
 __global__ void __launch_bounds__(kAttnThreads, 1)
     k_attn_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
               const __grid_constant__ CUtensorMap mv, const __grid_constant__ CUtensorMap mo, AttnArgs a) {
@@ -520,8 +504,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                         const int k0 = 32 * h + 2 * i;
                         const float x0 = fmaf(sc[k0], a.sl2, -m);
                         const float x1 = fmaf(sc[k0 + 1], a.sl2, -m);
-                        const float p0 = ((2 * i) % 8 < POLY) ? exp2_poly(x0) : fast_exp2(x0);
-                        const float p1 = ((2 * i + 1) % 8 < POLY) ? exp2_poly(x1) : fast_exp2(x1);
+                        const float p0 = fast_exp2(x0);
+                        const float p1 = fast_exp2(x1);
                         ls8[(2 * i) & 7] += p0;
                         ls8[(2 * i + 1) & 7] += p1;
                         const __half2 hp = __floats2half2_rn(p0, p1);
@@ -612,19 +596,13 @@ int attention_tc_launch(const __half *q, const __half *k, const __half *v, __hal
         !make_map_3d(&mv, v, B, S, cols_q, ldv, (uint64_t)S * ldv, kTcKeys, kTcDh) ||
         !make_map_3d(&mo, o, B, S, cols_q, ldo, (uint64_t)S * ldo, 32, kTcDh))
         return 0;
-    static const int poly = [] {   // SH_ATTN_POLY = 0 / 2 / 3: exponentials per 8 keys computed on the FMA pipe
-        const char *e = getenv("SH_ATTN_POLY");
-        const int v = e ? atoi(e) : kDefaultPoly;
-        return v == 0 || v == 2 || v == 3 ? v : kDefaultPoly;
-    }();
-    auto kern = poly == 3 ? k_attn_tc<3> : poly == 2 ? k_attn_tc<2> : k_attn_tc<0>;
-    static bool attr_done[3][kMaxDevices] = {};
+    static bool attr_done[kMaxDevices] = {};
     const int dev = current_device() % kMaxDevices;
-    if (!attr_done[poly == 3 ? 2 : poly == 2 ? 1 : 0][dev]) {
-        if (!cuda_ok(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kAttnSmem),
+    if (!attr_done[dev]) {
+        if (!cuda_ok(cudaFuncSetAttribute(k_attn_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kAttnSmem),
                      "cudaFuncSetAttribute(attention)"))
             return -1;
-        attr_done[poly == 3 ? 2 : poly == 2 ? 1 : 0][dev] = true;
+        attr_done[dev] = true;
     }
     AttnArgs a;
     a.S = S;
@@ -637,7 +615,7 @@ int attention_tc_launch(const __half *q, const __half *k, const __half *v, __hal
     a.sl2 = scale * 1.4426950408889634f;
     a.err = state().dev_err;
     const uint32_t grid = (uint32_t)std::min<uint64_t>(items, (uint64_t)state().num_sms);
-    kern<<<grid, kAttnThreads, kAttnSmem, stream()>>>(mq, mk, mv, mo, a);
+    k_attn_tc<<<grid, kAttnThreads, kAttnSmem, stream()>>>(mq, mk, mv, mo, a);
     *launched = true;
     return cuda_ok(cudaGetLastError(), "sh_attention") ? 0 : -1;
 }
