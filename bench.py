@@ -6,7 +6,8 @@
 Workload: 12 pre-LN SigLIP-base layers (S=256, D=768, 12 heads x 64, FFN 3072, tanh-GELU,
 scale 1/8, eps 1e-6), a global batch of 512 sequences sharded data-parallel over the N ranks (B = 512 / N per GPU,
 weights replicated: every rank generates the same per-layer N(0, 0.02) weights from the same LCG seeds; x ~ N(0,1)).
-One step = one forward pass over the rank's shard, 84 library launches replayed from a CUDA graph. The activations
+One step = one forward pass over the rank's shard, 84 library launches replayed from a CUDA graph (--ln-fold: 61, the
+input's row statistics, then per layer 5 launches with both LayerNorms folded into the GEMMs). The activations
 (201 MB per tensor at B=512) are larger than the 126 MB L2, so no flush is needed between steps.
 
 One JSON line on rank 0 (the contract of this repository's driver): `value` is the whole-job images/s with the
@@ -179,6 +180,21 @@ def setup_encoder(rt, B: int, rank: int, nlayers: int = NLAYERS):
     return layers, act, x_in
 
 
+def schedule_maker(rt, act, layers, M: int, fold: bool):
+    """(x_in, x_out) -> (calls of one forward pass, result address). By default the 7-launch layer (separate
+    LayerNorm kernels); with --ln-fold both LayerNorms of every layer are folded into the GEMMs that consume them
+    (sh_cuda_gemm_ln: 1 + 5 launches per layer after a one-time weight transform). The folded form measured ~1 %
+    slower at B = 512: the GEMM epilogues, already as long as the main loops, absorb more than the LayerNorm kernels
+    cost."""
+    from softhier_cuda import encoder
+    lib = rt.lib
+    if not fold:
+        return lambda xi, xo: encoder.encoder_schedule(lib, act, layers, H, EPS, SCALE, xi, xo)
+    folded = [encoder.fold_layer_norms(rt, w, D, F) for w in layers]
+    stats = encoder.alloc_row_stats(rt, M, D)
+    return lambda xi, xo: encoder.encoder_schedule_folded(lib, act, folded, stats, H, EPS, SCALE, xi, xo)
+
+
 def run_ours(args, rank: int, world: int, local: int) -> dict | None:
     import torch
     from softhier_cuda import encoder
@@ -189,12 +205,14 @@ def run_ours(args, rank: int, world: int, local: int) -> dict | None:
         raise SystemExit(f"global batch {GLOBAL_BATCH} does not split over {world} ranks")
     B = GLOBAL_BATCH // world
     M = B * S
-    arena = (17 * M * D + (M * F - M * D) + NLAYERS * (4 * D * D + 2 * D * F + 10 * F)) * 2 + (256 << 20)
+    arena = ((17 * M * D + (M * F - M * D) + NLAYERS * (7 * D * D + 3 * D * F + 16 * F)) * 2 + 2 * M * (D // 64) * 8
+             + (256 << 20))
     rt = Runtime.open(local, arena_bytes=arena)
     lib = rt.lib
     layers, act, x_in = setup_encoder(rt, B, rank)
+    make_schedule = schedule_maker(rt, act, layers, B * S, args.ln_fold)
     rt.check()
-    sched, res = encoder.encoder_schedule(lib, act, layers, H, EPS, SCALE, x_in)
+    sched, res = make_schedule(x_in, None)
     stream = torch.cuda.Stream(device=local)
     rt.activate(stream)
 
@@ -279,7 +297,7 @@ def run_ours(args, rank: int, world: int, local: int) -> dict | None:
     slots_out = [rt.alloc(M, D), rt.alloc(M, D)]
     slot_step = []
     for sl in range(2):
-        sched_s, _ = encoder.encoder_schedule(lib, act, layers, H, EPS, SCALE, slots_in[sl], slots_out[sl])
+        sched_s, _ = make_schedule(slots_in[sl], slots_out[sl])
 
         def enqueue_s(sched_s=sched_s):
             for kind, fn in sched_s:
@@ -376,7 +394,7 @@ def run_ours(args, rank: int, world: int, local: int) -> dict | None:
         "data": "synthetic (seeded LCG: x N(0,1), weights N(0,0.02), zero biases, gamma 1, beta 0)",
         "config": {"workload": "SigLIP-base 12-layer encoder forward (BASELINE config 5)", "global_batch": GLOBAL_BATCH,
                    "per_gpu_batch": B, "seq_len": S, "d_model": D, "ffn": F, "heads": H, "layers": NLAYERS,
-                   "parallelism": f"dp{world}", "cuda_graph": graph is not None,
+                   "parallelism": f"dp{world}", "cuda_graph": graph is not None, "ln_fold": args.ln_fold,
                    "l2": "inputs larger than L2 (201 MB per activation tensor at B=512), no flush"},
         "e2e": {"value": round(e2e_value, 1), "unit": "images/s", "h2d_bytes_per_step": M * D * 2,
                 "d2h_bytes_per_step": M * D * 2, "steps": e2e_steps},
@@ -577,10 +595,10 @@ def run_layer(args, local: int) -> dict:
     import torch
     from softhier_cuda import encoder
     from softhier_cuda.runtime import Runtime
-    rt = Runtime.open(local, arena_bytes=64 << 20)
+    rt = Runtime.open(local, arena_bytes=96 << 20)
     lib = rt.lib
     layers, act, x_in = setup_encoder(rt, 1, 0, nlayers=1)
-    sched, _ = encoder.encoder_schedule(lib, act, layers, H, EPS, SCALE, x_in)
+    sched, _ = schedule_maker(rt, act, layers, S, args.ln_fold)(x_in, None)
     stream = torch.cuda.Stream(device=local)
     rt.activate(stream)
 
@@ -612,7 +630,7 @@ def run_layer(args, local: int) -> dict:
             "peak": f"{src} bf16 burst {pk['bf16_tflops']} TFLOP/s", "dtype": "f16", "launches": len(sched),
             "reference_gvsoc_ms_per_layer": 1.920,
             "config": {"workload": "BASELINE config 3: one SigLIP-base layer, B=1, S=256, D=768, 12 heads, FFN 3072",
-                       "cuda_graph": True}}
+                       "cuda_graph": True, "ln_fold": args.ln_fold}}
 
 
 def run_rowops(args, local: int) -> dict:
@@ -746,6 +764,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--ln-fold", action="store_true", help="fold both LayerNorms of each layer into its GEMMs")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-images", type=int, default=2)
     ap.add_argument("--debug", action="store_true")

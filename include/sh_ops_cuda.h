@@ -57,6 +57,29 @@ uint32_t sh_cuda_abi_version(void);                 /* 1 */
 int sh_cuda_gemm(uint64_t x, uint64_t w, uint64_t z, uint32_t M, uint32_t N, uint32_t K, uint32_t ldx, uint32_t ldw,
                  uint32_t ldz, uint64_t bias, uint64_t residual, uint32_t ldr, uint32_t flags, uint32_t splits);
 
+/* ---- GEMM with LayerNorm folded in, and row statistics out ----------------------------------------------------------
+ * No counterpart in the reference: the library form of "layernorm -> gemm" (frontend/siglip.py:136-162) without
+ * materialising the normalised rows. With W' = diag(gamma) W, colsum = 1^T W' (fp32, 1 x N) and
+ * d = beta W + bias (fp16, 1 x N, passed as `bias` with SH_EPI_BIAS),
+ *     layernorm(X) W + bias = rstd_r (X W' - mean_r colsum) + d,
+ * so the GEMM reads raw X. Flags (in addition to sh_cuda_gemm's):
+ *   SH_EPI_LN_IN     t = rstd_r (acc - mean_r colsum[col]) first; mean_r / rstd_r (eps `ln_eps`) come from
+ *                    `ln_stats`: K / 64 (sum, sum of squares) fp32 pairs per row, K % 64 == 0
+ *   SH_EPI_STATS_OUT write N / 64 (sum, sum of squares) fp32 pairs per row of the final outputs (before fp16
+ *                    rounding) to `stats_out`, N % 64 == 0: the next GEMM's ln_stats
+ * No split-K; 16-byte aligned operands. Returns 0 or -1 (reason printed). */
+#define SH_EPI_LN_IN      0x40u
+#define SH_EPI_STATS_OUT  0x80u
+int sh_cuda_gemm_ln(uint64_t x, uint64_t w, uint64_t z, uint32_t M, uint32_t N, uint32_t K, uint32_t ldx,
+                    uint32_t ldw, uint32_t ldz, uint64_t bias, uint64_t residual, uint32_t ldr, uint32_t flags,
+                    uint64_t ln_stats, uint64_t ln_colsum, float ln_eps, uint64_t stats_out);
+/* (sum, sum of squares) of every 64 columns of each row of X (cols % 64 == 0): the row statistics of a matrix no
+ * GEMM produced (the encoder's input). Returns 0 or -1. */
+int sh_cuda_row_stats(uint64_t x, uint32_t rows, uint32_t cols, uint32_t ld, uint64_t stats_out);
+/* dst[r, c] = src[r, c] * gamma[r] in fp16 (W' = diag(gamma) W for sh_cuda_gemm_ln). Returns 0 or -1. */
+int sh_cuda_scale_rows(uint64_t dst, uint64_t src, uint32_t rows, uint32_t cols, uint32_t ld_src, uint32_t ld_dst,
+                       uint64_t gamma);
+
 /* ---- split-K GEMM without allocation -------------------------------------------------------------------------
  * No counterpart in the reference. The same computation, arguments and return codes as sh_cuda_gemm, for callers
  * that cannot let the library call cudaMalloc (a host whose own pool owns all device memory, or a loop that cannot

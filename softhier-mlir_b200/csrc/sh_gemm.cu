@@ -54,7 +54,32 @@ struct GemmArgs {
     float *ws;
     uint32_t *counters;
     int *err;
+    // LayerNorm folded into the GEMM (SH_EPI_LN_IN): X holds raw rows whose statistics arrive as ln_parts partial
+    // (sum, sum of squares) pairs per row; t = rstd (acc - mean colsum[col]) before the bias
+    const float2 *ln_stats;
+    const float *ln_colsum;
+    uint32_t ln_parts;
+    float ln_eps;
+    // SH_EPI_STATS_OUT: (sum, sum of squares) of each row's outputs per 64 columns, N / 64 pairs per row
+    float2 *stats_out;
 };
+
+// mean and 1 / sqrt(var + eps) of a row of K values from its partial sums (SH_EPI_LN_IN)
+__device__ __forceinline__ float2 ln_row(const GemmArgs &a, uint32_t row) {
+    if (!(a.flags & SH_EPI_LN_IN) || row >= a.M) return make_float2(0.f, 1.f);
+    const float2 *p = a.ln_stats + (size_t)row * a.ln_parts;
+    float s1[4] = {0.f, 0.f, 0.f, 0.f}, s2[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+    for (uint32_t i = 0; i < a.ln_parts; ++i) {
+        const float2 q = p[i];
+        s1[i & 3] += q.x;
+        s2[i & 3] += q.y;
+    }
+    const float inv_k = 1.f / (float)a.K;
+    const float mean = ((s1[0] + s1[1]) + (s1[2] + s1[3])) * inv_k;
+    const float var = fmaxf(((s2[0] + s2[1]) + (s2[2] + s2[3])) * inv_k - mean * mean, 0.f);
+    return make_float2(mean, rsqrtf(var + a.ln_eps));
+}
 
 // Barrier of the four epilogue warps on an mbarrier (count 4), so that it is bounded like every other wait.
 __device__ __forceinline__ bool epi_sync(uint64_t *bar, uint32_t &phase, volatile int *abort, int *err) {
@@ -165,8 +190,19 @@ __device__ __forceinline__ void add8(float *v, const uint4 &raw) {
 }
 // fused math of 32 consecutive in-range columns of one row on the 16-byte path; `res` holds the residual
 __device__ __forceinline__ void epi_math32(const GemmArgs &a, uint32_t row, uint32_t col, float (&v)[32],
-                                           const uint4 (&res)[4]) {
+                                           const uint4 (&res)[4], float2 ln) {
     const uint32_t f = a.flags;
+    if (f & SH_EPI_LN_IN) {
+        const float4 *cs = reinterpret_cast<const float4 *>(a.ln_colsum + col);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            const float4 c = __ldg(cs + q);
+            v[4 * q] = ln.y * fmaf(-ln.x, c.x, v[4 * q]);
+            v[4 * q + 1] = ln.y * fmaf(-ln.x, c.y, v[4 * q + 1]);
+            v[4 * q + 2] = ln.y * fmaf(-ln.x, c.z, v[4 * q + 2]);
+            v[4 * q + 3] = ln.y * fmaf(-ln.x, c.w, v[4 * q + 3]);
+        }
+    }
     if (f & SH_EPI_ACCUMULATE) {
         uint4 old[4];
         load32(a.z + (size_t)row * a.ldz + col, old);
@@ -188,7 +224,8 @@ __device__ __forceinline__ void epi_math32(const GemmArgs &a, uint32_t row, uint
 }
 
 // fused math of 32 columns of one row whose loads may leave the matrix (guarded, element by element)
-__device__ __forceinline__ void epi_math_guarded(const GemmArgs &a, uint32_t row, uint32_t col, float (&v)[32]) {
+__device__ __forceinline__ void epi_math_guarded(const GemmArgs &a, uint32_t row, uint32_t col, float (&v)[32],
+                                                 float2 ln) {
     if (row >= a.M) return;
     const uint32_t f = a.flags;
 #pragma unroll
@@ -196,6 +233,7 @@ __device__ __forceinline__ void epi_math_guarded(const GemmArgs &a, uint32_t row
         const uint32_t c = col + i;
         if (c >= a.N) continue;
         float t = v[i];
+        if (f & SH_EPI_LN_IN) t = ln.y * fmaf(-ln.x, a.ln_colsum[c], t);
         if (f & SH_EPI_ACCUMULATE) t += __half2float(a.z[(size_t)row * a.ldz + c]);
         if (f & SH_EPI_BIAS) t += __half2float(a.bias[c]);
         if (f & SH_EPI_GELU) t = gelu_fast(t);
@@ -209,13 +247,29 @@ __device__ __forceinline__ void epi_math_guarded(const GemmArgs &a, uint32_t row
 // by one TMA store, or every thread stores its row directly (fp32 outputs, unaligned operands).
 __device__ __forceinline__ void epi_chunk(const GemmArgs &a, const CUtensorMap *mz, uint8_t *stg, uint32_t &nst,
                                           uint32_t row, uint32_t row_base, uint32_t col, float (&v)[32],
-                                          const uint4 (&res)[4], uint32_t lane) {
+                                          const uint4 (&res)[4], uint32_t lane, float2 ln, float2 &st) {
     const bool inb = a.vec && row < a.M && col + 32 <= a.N;
     if (a.tma_store) {
         if (inb)
-            epi_math32(a, row, col, v, res);
+            epi_math32(a, row, col, v, res, ln);
         else
-            epi_math_guarded(a, row, col, v);
+            epi_math_guarded(a, row, col, v, ln);
+        if ((a.flags & SH_EPI_STATS_OUT) && row < a.M && col < a.N) {   // N % 64 == 0: whole chunks only
+            float s1 = 0.f, s2 = 0.f, s1b = 0.f, s2b = 0.f;
+#pragma unroll
+            for (int i = 0; i < 32; i += 2) {
+                s1 += v[i];
+                s2 = fmaf(v[i], v[i], s2);
+                s1b += v[i + 1];
+                s2b = fmaf(v[i + 1], v[i + 1], s2b);
+            }
+            st.x += s1 + s1b;
+            st.y += s2 + s2b;
+            if (col & 32) {   // second chunk of a 64-column group
+                a.stats_out[(size_t)row * (a.N / 64) + col / 64] = st;
+                st = make_float2(0.f, 0.f);
+            }
+        }
         uint8_t *buf = stg + (nst & 1u) * 2048;
         if (lane == 0) bulk_wait_read1();     // the store issued from this buffer two chunks ago has read it
         __syncwarp();
@@ -235,7 +289,7 @@ __device__ __forceinline__ void epi_chunk(const GemmArgs &a, const CUtensorMap *
         }
         ++nst;
     } else if (inb && !(a.flags & (SH_EPI_F32_OUT | SH_EPI_ACC_F32_IN))) {
-        epi_math32(a, row, col, v, res);
+        epi_math32(a, row, col, v, res, ln);
         __half *zp = a.z + (size_t)row * a.ldz + col;
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
@@ -404,6 +458,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint4 res[4] = {};
             const bool res_vec = want_res && a.vec && row < a.M;
             if (res_vec && a.splits == 1 && col0 + 32 <= a.N) load32(a.resid + (size_t)row * a.ldr + col0, res);
+            const float2 ln = ln_row(a, row);   // LayerNorm statistics of this row (SH_EPI_LN_IN)
+            float2 st = make_float2(0.f, 0.f);
             if (!mbar_wait(&tfull[acc], acc_phase, abort, a.err)) break;
             tc_fence_after();
             const uint32_t taddr = tmem_base + ((quarter * 32u) << 16) + acc * BN + half * HB;
@@ -434,7 +490,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                 for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
                 if (!a.tma_store || (row_base < a.M && col < a.N))
-                    epi_chunk(a, &map_z, stg, nst, row, row_base, col, v, res, lane);
+                    epi_chunk(a, &map_z, stg, nst, row, row_base, col, v, res, lane, ln, st);
 #pragma unroll
                 for (int i = 0; i < 4; ++i) res[i] = nres[i];
             }
@@ -484,7 +540,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const uint32_t col = col0 + c * 32;
                         uint4 res[4] = {};
                         if (res_vec && col + 32 <= a.N) load32(a.resid + (size_t)row * a.ldr + col, res);
-                        epi_chunk(a, &map_z, stg, nst, row, row_base, col, v, res, lane);
+                        epi_chunk(a, &map_z, stg, nst, row, row_base, col, v, res, lane, ln, st);
                     }
                 }
                 // last_flag is rewritten for the next tile only after every warp has read it
@@ -672,6 +728,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
             uint4 res[4] = {};
             const bool res_vec = want_res && a.vec && row < a.M;
             if (res_vec && col0 + 32 <= a.N) load32(a.resid + (size_t)row * a.ldr + col0, res);
+            const float2 ln = ln_row(a, row);
+            float2 st = make_float2(0.f, 0.f);
             if (!mbar_wait(&tfull[acc], acc_phase, abort, a.err)) break;
             tc_fence_after();
             const uint32_t taddr = tmem_base + ((quarter * 32u) << 16) + acc * BN + half * HB;
@@ -688,7 +746,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
 #pragma unroll
                 for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
                 if (!a.tma_store || (row_base < a.M && col < a.N))
-                    epi_chunk(a, &map_z, stg, nst, row, row_base, col, v, res, lane);
+                    epi_chunk(a, &map_z, stg, nst, row, row_base, col, v, res, lane, ln, st);
 #pragma unroll
                 for (int i = 0; i < 4; ++i) res[i] = nres[i];
             }
@@ -776,12 +834,13 @@ struct Plan {
     uint32_t tiles_m = 0, tiles_n = 0, k_blocks = 0, splits = 1, kb_per_split = 0;
 };
 
-Plan make_plan(uint32_t M, uint32_t N, uint32_t K, uint32_t splits_req, int num_sms) {
+Plan make_plan(uint32_t M, uint32_t N, uint32_t K, uint32_t splits_req, int num_sms, int min_bn = 64) {
     Plan p;
     p.bn = N > 128 ? 256 : (N > 64 ? 128 : 64);
+    if (p.bn < min_bn) p.bn = min_bn;
     p.tiles_m = (M + BM - 1) / BM;
     // narrower tiles when the wide ones leave most SMs idle
-    while (p.bn > 64 && (uint64_t)p.tiles_m * ((N + p.bn - 1) / p.bn) * 2 < (uint64_t)num_sms) p.bn >>= 1;
+    while (p.bn > min_bn && (uint64_t)p.tiles_m * ((N + p.bn - 1) / p.bn) * 2 < (uint64_t)num_sms) p.bn >>= 1;
     p.tiles_n = (N + p.bn - 1) / p.bn;
     p.k_blocks = (K + BK - 1) / BK;
     const uint32_t tiles = p.tiles_m * p.tiles_n;
@@ -848,10 +907,17 @@ uint32_t smem_of(int bn) {
 
 namespace sh {
 
-// Shared by sh_gemm / sh_gemm_mesh / sh_gemm_xmcast_ex / sh_cuda_gemm.
+struct LnFold {          // the extra operands of sh_cuda_gemm_ln
+    uint64_t stats;      // K / 64 (sum, sum of squares) pairs per row of X
+    uint64_t colsum;     // 1 x N fp32: column sums of diag(gamma) W
+    float eps;
+    uint64_t stats_out;  // N / 64 pairs per output row
+};
+
+// Shared by sh_gemm / sh_gemm_mesh / sh_gemm_xmcast_ex / sh_cuda_gemm / sh_cuda_gemm_ln (`ln` non-null).
 int gemm_run(uint64_t x, uint64_t w, uint64_t z, uint32_t M, uint32_t N, uint32_t K, uint32_t ldx, uint32_t ldw,
              uint32_t ldz, uint64_t bias, uint64_t resid, uint32_t ldr, uint32_t flags, uint32_t splits_req,
-             const char *name) {
+             const char *name, const LnFold *ln) {
     if (M == 0 || N == 0) return 0;
     if (!x || !w || !z || ldx < K || ldw < N || ldz < N || ((flags & SH_EPI_BIAS) && !bias) ||
         ((flags & (SH_EPI_RESIDUAL | SH_EPI_ACC_F32_IN)) && (!resid || ldr < N)) ||
@@ -879,6 +945,27 @@ int gemm_run(uint64_t x, uint64_t w, uint64_t z, uint32_t M, uint32_t N, uint32_
 
     const bool tc = !(flags & SH_GEMM_SIMT) && K > 0 && aligned16(x) && aligned16(w) && ldx % 8 == 0 &&
                     ldw % 8 == 0 && encode_tiled() != nullptr;
+    int min_bn = 64;
+    if (ln) {
+        const uint32_t lf = flags & (SH_EPI_LN_IN | SH_EPI_STATS_OUT);
+        const bool ok = tc && a.vec && !(flags & (SH_EPI_F32_OUT | SH_EPI_ACC_F32_IN | SH_EPI_ACCUMULATE)) &&
+                        (!(lf & SH_EPI_LN_IN) || (ln->stats && aligned16(ln->colsum) && K % 64 == 0)) &&
+                        (!(lf & SH_EPI_STATS_OUT) || (ln->stats_out && N % 64 == 0));
+        if (!ok) {
+            set_error(-1, "[%s] LayerNorm folding needs 16-byte aligned fp16 operands, K %% 64 == 0 (LN in), "
+                          "N %% 64 == 0 (stats out) and no accumulate / fp32 modes: %ux%ux%u flags %#x",
+                      name, M, N, K, flags);
+            return -1;
+        }
+        a.flags |= lf;
+        a.ln_stats = (const float2 *)ln->stats;
+        a.ln_colsum = (const float *)ln->colsum;
+        a.ln_parts = K / 64;
+        a.ln_eps = ln->eps;
+        a.stats_out = (float2 *)ln->stats_out;
+        splits_req = 1;
+        if (lf & SH_EPI_STATS_OUT) min_bn = 128;   // each epilogue thread covers whole 64-column groups
+    }
     if (!tc) {
         dim3 grid((N + 63) / 64, (M + 63) / 64);
         if (grid.y > 65535u) {
@@ -888,7 +975,7 @@ int gemm_run(uint64_t x, uint64_t w, uint64_t z, uint32_t M, uint32_t N, uint32_
         k_gemm_simt<<<grid, 256, 0, st>>>((const __half *)x, (const __half *)w, ldx, ldw, a);
         return cuda_ok(cudaGetLastError(), name) ? 0 : -1;
     }
-    Plan p = make_plan(M, N, K, splits_req, s.num_sms);
+    Plan p = make_plan(M, N, K, splits_req, s.num_sms, min_bn);
     a.tiles_n = p.tiles_n;
     a.num_tiles = p.tiles_m * p.tiles_n;
     a.k_blocks = p.k_blocks;
@@ -910,8 +997,13 @@ int gemm_run(uint64_t x, uint64_t w, uint64_t z, uint32_t M, uint32_t N, uint32_
         const char *e = getenv("SH_GEMM_TMA_STORE");
         return !(e && atoi(e) == 0);
     }();
-    a.tma_store = tma_store_env && a.vec && p.splits == 1 && !(a.flags & (SH_EPI_F32_OUT | SH_EPI_ACC_F32_IN)) &&
+    a.tma_store = (tma_store_env || ln) && a.vec && p.splits == 1 &&
+                  !(a.flags & (SH_EPI_F32_OUT | SH_EPI_ACC_F32_IN)) &&
                   make_map_2d_sw(&mz, (const void *)z, M, N, ldz, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B);
+    if (ln && !a.tma_store) {   // the folded epilogue runs on the staged-store path only
+        set_error(-1, "[%s] cuTensorMapEncodeTiled failed for the output of %ux%ux%u", name, M, N, K);
+        return -1;
+    }
     if (!a.tma_store) mz = mx;   // not read by the kernel
     if (p.pair) return launch_pair<256>(p, mx, mw, mz, a, st);
     switch (p.bn) {
@@ -958,7 +1050,8 @@ int sh_gemm(uint64_t x, uint64_t w, uint64_t z, uint32_t M, uint32_t N, uint32_t
         sh::set_error(-3, "[sh_gemm] fmt %u: only SH_FP16 runs on this backend", c.fmt);
         return -3;
     }
-    return sh::gemm_run(x, w, z, M, N, K, ldx, ldw, ldz, 0, 0, 0, c.accumulate ? SH_EPI_ACCUMULATE : 0, 0, "sh_gemm");
+    return sh::gemm_run(x, w, z, M, N, K, ldx, ldw, ldz, 0, 0, 0, c.accumulate ? SH_EPI_ACCUMULATE : 0, 0, "sh_gemm",
+                        nullptr);
 }
 
 int sh_gemm_mesh(uint64_t x, uint64_t w, uint64_t z, uint32_t M, uint32_t N, uint32_t K, uint32_t ldx, uint32_t ldw,
@@ -975,7 +1068,7 @@ int sh_gemm_mesh(uint64_t x, uint64_t w, uint64_t z, uint32_t M, uint32_t N, uin
         return -3;
     }
     return sh::gemm_run(x, w, z, M, N, K, ldx, ldw, ldz, 0, 0, 0, c.accumulate ? SH_EPI_ACCUMULATE : 0, 0,
-                        "sh_gemm_mesh");
+                        "sh_gemm_mesh", nullptr);
 }
 
 uint32_t sh_gemm_xmcast_l1_bytes(uint32_t M, uint32_t N, uint32_t K, const sh_gemm_cfg *cfg, uint32_t) {
@@ -1003,7 +1096,7 @@ int sh_gemm_xmcast_ex(uint64_t x, uint64_t w, uint64_t z, uint32_t M, uint32_t N
         return rc;
     }
     return sh::gemm_run(x, w, z, M, N, K, ldx, ldw, ldz, 0, 0, 0, c.accumulate ? SH_EPI_ACCUMULATE : 0, 0,
-                        "sh_gemm_xmcast");
+                        "sh_gemm_xmcast", nullptr);
 }
 
 int sh_gemm_xmcast(uint64_t x, uint64_t w, uint64_t z, uint32_t M, uint32_t N, uint32_t K, uint32_t ldx, uint32_t ldw,
@@ -1013,7 +1106,16 @@ int sh_gemm_xmcast(uint64_t x, uint64_t w, uint64_t z, uint32_t M, uint32_t N, u
 
 int sh_cuda_gemm(uint64_t x, uint64_t w, uint64_t z, uint32_t M, uint32_t N, uint32_t K, uint32_t ldx, uint32_t ldw,
                  uint32_t ldz, uint64_t bias, uint64_t residual, uint32_t ldr, uint32_t flags, uint32_t splits) {
-    return sh::gemm_run(x, w, z, M, N, K, ldx, ldw, ldz, bias, residual, ldr, flags, splits, "sh_cuda_gemm");
+    return sh::gemm_run(x, w, z, M, N, K, ldx, ldw, ldz, bias, residual, ldr, flags, splits, "sh_cuda_gemm",
+                        nullptr);
+}
+
+int sh_cuda_gemm_ln(uint64_t x, uint64_t w, uint64_t z, uint32_t M, uint32_t N, uint32_t K, uint32_t ldx,
+                    uint32_t ldw, uint32_t ldz, uint64_t bias, uint64_t residual, uint32_t ldr, uint32_t flags,
+                    uint64_t ln_stats, uint64_t ln_colsum, float ln_eps, uint64_t stats_out) {
+    const sh::LnFold ln{ln_stats, ln_colsum, ln_eps, stats_out};
+    return sh::gemm_run(x, w, z, M, N, K, ldx, ldw, ldz, bias, residual, ldr,
+                        flags & ~(uint32_t)SH_GEMM_SIMT, 1, "sh_cuda_gemm_ln", &ln);
 }
 
 }  // extern "C"

@@ -516,6 +516,41 @@ void sm_vec_launch(uint64_t y, uint64_t x, uint32_t rows, uint32_t cols, uint32_
 
 }  // namespace
 
+namespace {
+
+// (sum, sum of squares) of each 64-column group of a row (one thread per group; the format sh_cuda_gemm_ln reads)
+__global__ void __launch_bounds__(256) k_row_stats(const __half *x, uint32_t rows, uint32_t parts, uint32_t ld,
+                                                   float2 *out) {
+    const uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= (uint64_t)rows * parts) return;
+    const uint32_t r = (uint32_t)(t / parts), g = (uint32_t)(t % parts);
+    const uint4 *p = reinterpret_cast<const uint4 *>(x + (size_t)r * ld + (size_t)g * 64);
+    float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const uint4 u = __ldg(p + i);
+        const __half2 *h = reinterpret_cast<const __half2 *>(&u);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float2 f = __half22float2(h[j]);
+            s1 += f.x + f.y;
+            s2 = fmaf(f.x, f.x, fmaf(f.y, f.y, s2));
+        }
+    }
+    out[t] = make_float2(s1, s2);
+}
+
+// dst[r, c] = src[r, c] * gamma[r] (fp16)
+__global__ void __launch_bounds__(256) k_scale_rows(__half *dst, const __half *src, uint32_t rows, uint32_t cols,
+                                                    uint32_t lds, uint32_t ldd, const __half *gamma) {
+    const uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= (uint64_t)rows * cols) return;
+    const uint32_t r = (uint32_t)(t / cols), c = (uint32_t)(t % cols);
+    dst[(size_t)r * ldd + c] = __float2half_rn(__half2float(src[(size_t)r * lds + c]) * __half2float(gamma[r]));
+}
+
+}  // namespace
+
 extern "C" {
 
 void sh_layernorm(uint64_t y, uint64_t x, uint64_t gamma, uint64_t beta, uint32_t rows, uint32_t cols, uint32_t ld,
@@ -589,6 +624,32 @@ void sh_transpose(uint64_t dst, uint64_t src, uint32_t rows, uint32_t cols, uint
                                                     vec);
     }
     sh::cuda_ok(cudaGetLastError(), "sh_transpose");
+}
+
+int sh_cuda_row_stats(uint64_t x, uint32_t rows, uint32_t cols, uint32_t ld, uint64_t stats_out) {
+    if (rows == 0) return 0;
+    if (!x || !stats_out || cols % 64 || cols == 0 || ld < cols || !vec_ok(x, ld)) {
+        sh::set_error(-1, "[sh_cuda_row_stats] %ux%u ld %u: need cols %% 64 == 0 and 16-byte aligned rows", rows,
+                      cols, ld);
+        return -1;
+    }
+    const uint64_t n = (uint64_t)rows * (cols / 64);
+    k_row_stats<<<(unsigned)((n + 255) / 256), 256, 0, sh::stream()>>>((const __half *)x, rows, cols / 64, ld,
+                                                                        (float2 *)stats_out);
+    return sh::cuda_ok(cudaGetLastError(), "sh_cuda_row_stats") ? 0 : -1;
+}
+
+int sh_cuda_scale_rows(uint64_t dst, uint64_t src, uint32_t rows, uint32_t cols, uint32_t ld_src, uint32_t ld_dst,
+                       uint64_t gamma) {
+    if (rows == 0 || cols == 0) return 0;
+    if (!dst || !src || !gamma || ld_src < cols || ld_dst < cols) {
+        sh::set_error(-1, "[sh_cuda_scale_rows] %ux%u ld %u / %u", rows, cols, ld_src, ld_dst);
+        return -1;
+    }
+    const uint64_t n = (uint64_t)rows * cols;
+    k_scale_rows<<<(unsigned)((n + 255) / 256), 256, 0, sh::stream()>>>((__half *)dst, (const __half *)src, rows,
+                                                                         cols, ld_src, ld_dst, (const __half *)gamma);
+    return sh::cuda_ok(cudaGetLastError(), "sh_cuda_scale_rows") ? 0 : -1;
 }
 
 }  // extern "C"

@@ -108,6 +108,83 @@ def layer_ops(lib, act: Activations, w: LayerWeights, heads: int, eps: float, sc
     ]
 
 
+# ---- LayerNorm folded into the GEMMs ----------------------------------------------------------------------------------
+@dataclass
+class FoldedWeights:
+    """A layer with LN1 folded into the QKV GEMM and LN2 into FC1 (sh_cuda_gemm_ln): w' = diag(gamma) w,
+    colsum = 1^T w' (fp32), bias' = beta w + bias (fp16)."""
+    wqkv: int
+    cqkv: int
+    dqkv: int
+    wo: int
+    bo: int
+    w1: int
+    c1: int
+    d1: int
+    w2: int
+    b2: int
+
+
+def fold_layer_norms(rt: Runtime, w: LayerWeights, D: int, F: int) -> FoldedWeights:
+    """Device-side weight transform (setup, not per step): both folds are GEMMs / row scalings on the library."""
+    lib, a = rt.lib, rt.alloc
+    ones = a(1, D)
+    lib.sh_test_fill_const_fp16(ones, 1, D, D, 0x3C00)
+    out = {}
+    for tag, wt, bias, g, be, n in (("qkv", w.wqkv, w.bqkv, w.g1, w.be1, 3 * D), ("1", w.w1, w.b1, w.g2, w.be2, F)):
+        wp, c, d = a(D, n), rt.alloc_bytes(4 * n), a(1, n)
+        rc = lib.sh_cuda_scale_rows(wp, wt, D, n, n, n, g)
+        rc = rc or lib.sh_cuda_gemm(ones, wp, c, 1, n, D, D, n, n, 0, 0, 0, L.EPI_F32_OUT, 1)
+        rc = rc or lib.sh_cuda_gemm(be, wt, d, 1, n, D, D, n, n, bias, 0, 0, L.EPI_BIAS, 1)
+        if rc:
+            raise RuntimeError(f"folding LayerNorm into the {tag} GEMM failed: {rc}")
+        out[tag] = (wp, c, d)
+    return FoldedWeights(wqkv=out["qkv"][0], cqkv=out["qkv"][1], dqkv=out["qkv"][2], wo=w.wo, bo=w.bo,
+                         w1=out["1"][0], c1=out["1"][1], d1=out["1"][2], w2=w.w2, b2=w.b2)
+
+
+def alloc_row_stats(rt: Runtime, M: int, D: int) -> tuple[int, int]:
+    """(stats of the residual stream x, stats of h): D / 64 fp32 (sum, sum of squares) pairs per row each."""
+    return rt.alloc_bytes(M * (D // 64) * 8), rt.alloc_bytes(M * (D // 64) * 8)
+
+
+def layer_ops_folded(lib, act: Activations, w: FoldedWeights, stats: tuple[int, int], heads: int, eps: float,
+                     scale: float, x: int, out: int) -> list[tuple[str, Callable[[], int]]]:
+    """The 5 launches of one layer with both LayerNorms folded: x's row statistics are in stats[0] (written by the
+    previous layer's FC2, or sh_cuda_row_stats for the first), the O projection writes h's into stats[1]."""
+    B, S, D, F = act.B, act.S, act.D, act.F
+    M = B * S
+    sx, sh = stats
+    g = lib.sh_cuda_gemm_ln
+    return [
+        ("gemm_qkv", lambda: g(x, w.wqkv, act.qkv, M, 3 * D, D, D, 3 * D, 3 * D, w.dqkv, 0, 0,
+                               L.EPI_BIAS | L.EPI_LN_IN, sx, w.cqkv, eps, 0)),
+        ("attention", lambda: lib.sh_cuda_attention_batched(act.qkv, act.qkv + 2 * D, act.qkv + 4 * D, act.o, S, D,
+                                                            heads, 3 * D, 3 * D, 3 * D, D, scale, B)),
+        ("gemm_o", lambda: g(act.o, w.wo, act.h, M, D, D, D, D, D, w.bo, x, D,
+                             L.EPI_BIAS | L.EPI_RESIDUAL | L.EPI_STATS_OUT, 0, 0, eps, sh)),
+        ("gemm_fc1", lambda: g(act.h, w.w1, act.g, M, F, D, D, F, F, w.d1, 0, 0,
+                               L.EPI_BIAS | L.EPI_GELU | L.EPI_LN_IN, sh, w.c1, eps, 0)),
+        ("gemm_fc2", lambda: g(act.g, w.w2, out, M, D, F, F, D, D, w.b2, act.h, D,
+                               L.EPI_BIAS | L.EPI_RESIDUAL | L.EPI_STATS_OUT, 0, 0, eps, sx)),
+    ]
+
+
+def encoder_schedule_folded(lib, act: Activations, layers: list[FoldedWeights], stats: tuple[int, int], heads: int,
+                            eps: float, scale: float, x_in: int | None = None,
+                            x_out: int | None = None) -> tuple[list[tuple[str, Callable[[], int]]], int]:
+    """encoder_schedule with the LayerNorms folded: one sh_cuda_row_stats of the input, then 5 launches per layer."""
+    M, D = act.B * act.S, act.D
+    cur = act.x if x_in is None else x_in
+    nxt = act.out
+    sched = [("row_stats", lambda x0=cur: lib.sh_cuda_row_stats(x0, M, D, D, stats[0]))]
+    for i, w in enumerate(layers):
+        dst = x_out if (x_out is not None and i == len(layers) - 1) else nxt
+        sched += layer_ops_folded(lib, act, w, stats, heads, eps, scale, cur, dst)
+        cur, nxt = dst, (act.x if nxt == act.out else act.out)
+    return sched, cur
+
+
 def op_work(kind: str, B: int, S: int, D: int, F: int, heads: int) -> tuple[float, float]:
     """(algorithmic FLOPs, algorithmic HBM bytes) of one launch of `kind` (fp16 = 2 B per element)."""
     M = B * S
@@ -123,6 +200,8 @@ def op_work(kind: str, B: int, S: int, D: int, F: int, heads: int) -> tuple[floa
         return 2.0 * M * F * D, 2.0 * (M * F + F * D + 2 * M * D + D)
     if kind == "attention":
         return 4.0 * B * S * S * D, 2.0 * 4 * M * D
+    if kind == "row_stats":
+        return 3.0 * M * D, 2.0 * M * D + 8.0 * M * (D // 64)
     raise KeyError(kind)
 
 

@@ -73,6 +73,9 @@ SIGNATURES: dict[str, tuple] = {
     "sh_cuda_last_error": (i32, []), "sh_cuda_last_error_string": (cp, []), "sh_cuda_device_error": (i32, []),
     "sh_cuda_num_sms": (i32, []), "sh_cuda_timer_last_ms": (f32, []), "sh_cuda_abi_version": (u32, []),
     "sh_cuda_gemm": (i32, [u64, u64, u64, u32, u32, u32, u32, u32, u32, u64, u64, u32, u32, u32]),
+    "sh_cuda_gemm_ln": (i32, [u64, u64, u64, u32, u32, u32, u32, u32, u32, u64, u64, u32, u32, u64, u64, f32, u64]),
+    "sh_cuda_row_stats": (i32, [u64, u32, u32, u32, u64]),
+    "sh_cuda_scale_rows": (i32, [u64, u64, u32, u32, u32, u32, u64]),
     "sh_cuda_add_layernorm": (None, [u64, u64, u64, u64, u64, u64, u32, u32, u32, f32]),
     "sh_cuda_attention_batched": (i32, [u64, u64, u64, u64, u32, u32, u32, u32, u32, u32, u32, f32, u32]),
     "sh_cuda_fill_normal_fp16": (None, [u64, u32, u32, u32, u32, f32, f32]),
@@ -86,6 +89,7 @@ SIGNATURES: dict[str, tuple] = {
 # sh_ops_cuda.h constants
 EPI_ACCUMULATE, EPI_BIAS, EPI_GELU, EPI_RESIDUAL, GEMM_SIMT = 0x1, 0x2, 0x4, 0x8, 0x100
 EPI_F32_OUT, EPI_ACC_F32_IN = 0x10, 0x20
+EPI_LN_IN, EPI_STATS_OUT = 0x40, 0x80
 SH_ALL = 0xFFFFFFFF
 SH_FP16, SH_FP8, SH_INT16, SH_INT8 = 0, 1, 2, 3
 SH_XM_AUTO, SH_XM_PANEL, SH_XM_WHOLE = 0, 1, 2
