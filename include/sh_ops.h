@@ -105,6 +105,27 @@ uint32_t sh_attention_l1_bytes(uint32_t S, uint32_t dh);
 uint32_t sh_attention_q_block(uint32_t S, uint32_t dh, uint32_t H, uint32_t P);   /* the reference's rule, 1 MB TCDM */
 uint32_t sh_attention_profile(uint32_t S, uint32_t dh, uint32_t phase);   /* no per-phase stamps here: 0 */
 
+/* ---- Llama-style decoder ops (sh_ops.h:277-304; runtime/sh_llm.inc.c) --------------------------------------
+ * Token masks: one uint16 class per position; query i attends key j iff tok[j] <= tok[i] (unsigned), SH_LLM_PAD
+ * marks padding, a PAD query row gets uniform probabilities. fp16 tensors, cols % 4 == 0 as in the reference. */
+#define SH_LLM_PAD 0xFFFFu                                                                  /* sh_ops.h:283 */
+void sh_rmsnorm(uint64_t y, uint64_t x, uint64_t gamma, uint32_t rows, uint32_t cols, uint32_t ld, float eps,
+                uint32_t cluster);                                                          /* sh_ops.h:284 */
+void sh_rope(uint64_t y, uint64_t x, uint64_t cos_sin, uint32_t rows, uint32_t cols, uint32_t ld, uint32_t ld_table,
+             uint32_t dh, uint32_t cluster);                                                /* sh_ops.h:288 */
+void sh_silu_mul(uint64_t y, uint64_t a, uint64_t b, uint32_t rows, uint32_t cols, uint32_t ld,
+                 uint32_t cluster);                                                         /* sh_ops.h:289 */
+void sh_softmax_masked(uint64_t y, uint64_t x, uint32_t rows, uint32_t cols, uint32_t ld, float scale,
+                       uint64_t tok_q, uint64_t tok_k, uint32_t cluster);                   /* sh_ops.h:292 */
+int sh_attention_head_masked(uint64_t q, uint64_t k, uint64_t v, uint64_t o, uint32_t S, uint32_t dh, uint32_t ldq,
+                             uint32_t ldk, uint32_t ldv, uint32_t ldo, float scale, uint64_t tok,
+                             uint32_t cluster);                                             /* sh_ops.h:294-295 */
+int sh_attention_gqa(uint64_t q, uint64_t k, uint64_t v, uint64_t o, uint32_t S, uint32_t D, uint32_t H, uint32_t Hkv,
+                     uint32_t ldq, uint32_t ldk, uint32_t ldv, uint32_t ldo, float scale, uint64_t tok,
+                     uint32_t cluster);                                                     /* sh_ops.h:299-300 */
+void sh_pixel_shuffle(uint64_t dst, uint64_t src, uint32_t grid, uint32_t D, uint32_t s,
+                      uint32_t cluster);                                                    /* sh_ops.h:303 */
+
 /* ---- test helpers (sh_ops.h:220-240) ---------------------------------------------------------------------- */
 void sh_test_fill_int_fp16(uint64_t a, uint32_t rows, uint32_t cols, uint32_t ld, uint32_t seed, int lo, int hi);
 void sh_test_fill_fp16(uint64_t a, uint32_t rows, uint32_t cols, uint32_t ld, uint32_t seed, int lo, int hi, float scale);

@@ -17,7 +17,7 @@
 namespace sh {
 int attention_tc_launch(const __half *q, const __half *k, const __half *v, __half *o, uint32_t S, uint32_t H,
                         uint32_t dh, uint32_t ldq, uint32_t ldk, uint32_t ldv, uint32_t ldo, float scale, uint32_t B,
-                        bool *launched);
+                        uint32_t kv_group, bool *launched);
 }
 
 namespace {
@@ -25,16 +25,23 @@ namespace {
 constexpr int kSimtRows = 128;   // query rows per CTA (one per thread)
 constexpr int kSimtKeys = 32;    // keys staged per step
 
+// kv_group query heads share one key/value head (grouped-query attention; 1 = multi-head). tok (nullable): one
+// uint16 class per position, query i attends key j iff tok[j] <= tok[i], a PAD (0xFFFF) query row averages every
+// value row (sh_ops.h:277-300).
 template <int DH>
 __global__ void __launch_bounds__(kSimtRows) k_attn_simt(const __half *q, const __half *k, const __half *v, __half *o,
                                                          uint32_t S, uint32_t dh, uint32_t ldq, uint32_t ldk,
-                                                         uint32_t ldv, uint32_t ldo, float scale_log2) {
+                                                         uint32_t ldv, uint32_t ldo, float scale_log2,
+                                                         uint32_t kv_group, const uint16_t *tok) {
     __shared__ float ks[kSimtKeys][DH];
     __shared__ float vs[kSimtKeys][DH];
+    __shared__ uint16_t ts[kSimtKeys];
     const uint32_t b = blockIdx.z, h = blockIdx.y;
     const uint32_t row = blockIdx.x * kSimtRows + threadIdx.x;
     const size_t r0 = (size_t)b * S;
-    const size_t col0 = (size_t)h * dh;
+    const size_t col0 = (size_t)h * dh, kcol0 = (size_t)(h / kv_group) * dh;
+    const uint32_t tq = (tok && row < S) ? tok[r0 + row] : 0u;
+    const bool pad_row = tok && tq == 0xFFFFu;
     float qr[DH], acc[DH];
     float m = -INFINITY, l = 0.f;
 #pragma unroll
@@ -46,9 +53,10 @@ __global__ void __launch_bounds__(kSimtRows) k_attn_simt(const __half *q, const 
         for (uint32_t i = threadIdx.x; i < kSimtKeys * DH; i += kSimtRows) {
             const uint32_t j = i / DH, d = i % DH;
             const bool in = kt + j < S && d < dh;
-            ks[j][d] = in ? __half2float(k[(r0 + kt + j) * ldk + col0 + d]) : 0.f;
-            vs[j][d] = in ? __half2float(v[(r0 + kt + j) * ldv + col0 + d]) : 0.f;
+            ks[j][d] = in ? __half2float(k[(r0 + kt + j) * ldk + kcol0 + d]) : 0.f;
+            vs[j][d] = in ? __half2float(v[(r0 + kt + j) * ldv + kcol0 + d]) : 0.f;
         }
+        if (tok && threadIdx.x < kSimtKeys) ts[threadIdx.x] = (kt + threadIdx.x < S) ? tok[r0 + kt + threadIdx.x] : 0;
         __syncthreads();
         const uint32_t nk = min((uint32_t)kSimtKeys, S - kt);
         float s[kSimtKeys];
@@ -58,17 +66,20 @@ __global__ void __launch_bounds__(kSimtRows) k_attn_simt(const __half *q, const 
             float t = 0.f;
 #pragma unroll
             for (int d = 0; d < DH; ++d) t += qr[d] * ks[j][d];
+            if (pad_row) t = 0.f;                                   // uniform over every key
+            else if (tok && ts[j] > tq) t = -INFINITY;              // key class above the query's
             s[j] = (j < (int)nk) ? t : -INFINITY;
             tmax = fmaxf(tmax, s[j]);
         }
         const float mn = fmaxf(m, tmax);
-        const float corr = exp2f(m - mn);
+        const float mref = (mn == -INFINITY) ? 0.f : mn;   // no attendable key yet (masked block): p = 0
+        const float corr = exp2f(m - mref);
         l *= corr;
 #pragma unroll
         for (int d = 0; d < DH; ++d) acc[d] *= corr;
 #pragma unroll
         for (int j = 0; j < kSimtKeys; ++j) {
-            const float p = exp2f(s[j] - mn);
+            const float p = exp2f(s[j] - mref);
             l += p;
 #pragma unroll
             for (int d = 0; d < DH; ++d) acc[d] += p * vs[j][d];
@@ -98,26 +109,30 @@ int check(uint32_t S, uint32_t dh, uint32_t sq) {   // sh_attention.inc.c:198-20
 }
 
 int run(uint64_t q, uint64_t k, uint64_t v, uint64_t o, uint32_t S, uint32_t H, uint32_t dh, uint32_t ldq,
-        uint32_t ldk, uint32_t ldv, uint32_t ldo, float scale, uint32_t B) {
+        uint32_t ldk, uint32_t ldv, uint32_t ldo, float scale, uint32_t B, uint32_t kv_group = 1,
+        uint64_t tok = 0, const char *name = "sh_attention") {
     if (S == 0 || H == 0 || B == 0) return 0;
     if (!q || !k || !v || !o) {
-        sh::set_error(-1, "[sh_attention] null operand");
+        sh::set_error(-1, "[%s] null operand", name);
         return -1;
     }
-    bool launched = false;
-    const int rc = sh::attention_tc_launch((const __half *)q, (const __half *)k, (const __half *)v, (__half *)o, S, H,
-                                           dh, ldq, ldk, ldv, ldo, scale, B, &launched);
-    if (launched || rc) return rc;
+    if (!tok) {   // the tensor-core kernel has no token mask
+        bool launched = false;
+        const int rc = sh::attention_tc_launch((const __half *)q, (const __half *)k, (const __half *)v, (__half *)o,
+                                               S, H, dh, ldq, ldk, ldv, ldo, scale, B, kv_group, &launched);
+        if (launched || rc) return rc;
+    }
     const float sl2 = scale * 1.4426950408889634f;
     dim3 grid((S + kSimtRows - 1) / kSimtRows, H, B);
     if (grid.y > 65535u || grid.z > 65535u) {
-        sh::set_error(-1, "[sh_attention] H=%u B=%u too large", H, B);
+        sh::set_error(-1, "[%s] H=%u B=%u too large", name, H, B);
         return -1;
     }
     cudaStream_t st = sh::stream();
 #define SH_ATTN_SIMT(DHT)                                                                                        \
     k_attn_simt<DHT><<<grid, kSimtRows, 0, st>>>((const __half *)q, (const __half *)k, (const __half *)v,        \
-                                                 (__half *)o, S, dh, ldq, ldk, ldv, ldo, sl2)
+                                                 (__half *)o, S, dh, ldq, ldk, ldv, ldo, sl2, kv_group,          \
+                                                 (const uint16_t *)tok)
     if (dh <= 16)
         SH_ATTN_SIMT(16);
     else if (dh <= 32)
@@ -127,11 +142,11 @@ int run(uint64_t q, uint64_t k, uint64_t v, uint64_t o, uint32_t S, uint32_t H, 
     else if (dh <= 128)
         SH_ATTN_SIMT(128);
     else {
-        sh::set_error(-1, "[sh_attention] dh=%u > 128 is not supported", dh);
+        sh::set_error(-1, "[%s] dh=%u > 128 is not supported", name, dh);
         return -1;
     }
 #undef SH_ATTN_SIMT
-    return sh::cuda_ok(cudaGetLastError(), "sh_attention") ? 0 : -1;
+    return sh::cuda_ok(cudaGetLastError(), name) ? 0 : -1;
 }
 
 }  // namespace
@@ -205,6 +220,27 @@ int sh_cuda_attention_batched(uint64_t q, uint64_t k, uint64_t v, uint64_t o, ui
     return run(q, k, v, o, S, H, dh, ldq, ldk, ldv, ldo, scale, B);
 }
 
+// One head with the decoder token mask (sh_ops.h:294-295, sh_llm.inc.c:258): the reference keeps the head in TCDM
+// (S <= 256); here any S.
+int sh_attention_head_masked(uint64_t q, uint64_t k, uint64_t v, uint64_t o, uint32_t S, uint32_t dh, uint32_t ldq,
+                             uint32_t ldk, uint32_t ldv, uint32_t ldo, float scale, uint64_t tok, uint32_t) {
+    if (check(S, dh, 4)) return -1;
+    return run(q, k, v, o, S, 1, dh, ldq, ldk, ldv, ldo, scale, 1, 1, tok, "sh_attention_head_masked");
+}
+
+// Grouped-query attention (sh_ops.h:296-300, sh_llm.inc.c:325-340): query head h reads key / value head
+// h / (H / Hkv); without a token mask and with dh = 64 it runs on the tensor-core kernel.
+int sh_attention_gqa(uint64_t q, uint64_t k, uint64_t v, uint64_t o, uint32_t S, uint32_t D, uint32_t H, uint32_t Hkv,
+                     uint32_t ldq, uint32_t ldk, uint32_t ldv, uint32_t ldo, float scale, uint64_t tok, uint32_t) {
+    const uint32_t dh = H ? D / H : 0;
+    if (H == 0 || Hkv == 0 || dh * H != D || H % Hkv) {
+        sh::set_error(-1, "[sh_attention_gqa] bad D=%u H=%u Hkv=%u", D, H, Hkv);
+        return -1;
+    }
+    if (check(S, dh, 4)) return -1;
+    return run(q, k, v, o, S, H, dh, ldq, ldk, ldv, ldo, scale, 1, H / Hkv, tok, "sh_attention_gqa");
+}
+
 }  // extern "C"
 
 // ================================================================================================================
@@ -243,7 +279,7 @@ constexpr uint32_t kAttnThreads = 320;
 constexpr float kRescaleLog2 = 8.f;
 
 struct AttnArgs {
-    uint32_t S, H, nkb, nqp, items;
+    uint32_t S, H, kv_group, nkb, nqp, items;
     float sl2;   // scale * log2(e)
     int *err;
 };
@@ -303,6 +339,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             for (uint32_t it = blockIdx.x; ok && it < a.items; it += gridDim.x) {
                 const uint32_t qp = it % a.nqp, bh = it / a.nqp;
                 const int32_t col = (int32_t)((bh % a.H) * kTcDh), b = (int32_t)(bh / a.H);
+                const int32_t kcol = (int32_t)(((bh % a.H) / a.kv_group) * kTcDh);   // grouped-query K / V head
                 if (!mbar_wait(&q_empty[qs], qph ^ 1u, abort, a.err)) break;
                 mbar_arrive_expect_tx(&q_full[qs], 2 * kTileBytes);
                 q_armed[qs] = qph;
@@ -320,9 +357,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                     }
                     uint8_t *kt = sm + kKvOff + st * 2 * kTileBytes;
                     mbar_arrive_expect_tx(&k_full[st], kTileBytes);
-                    tma_load_3d(kt, &mk, &k_full[st], col, (int32_t)(j * kTcKeys), b);
+                    tma_load_3d(kt, &mk, &k_full[st], kcol, (int32_t)(j * kTcKeys), b);
                     mbar_arrive_expect_tx(&v_full[st], kTileBytes);
-                    tma_load_3d(kt + kTileBytes, &mv, &v_full[st], col, (int32_t)(j * kTcKeys), b);
+                    tma_load_3d(kt + kTileBytes, &mv, &v_full[st], kcol, (int32_t)(j * kTcKeys), b);
                     kv_armed[st] = kph;
                     if (++st == kKvStages) {
                         st = 0;
@@ -584,16 +621,16 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 namespace sh {
 int attention_tc_launch(const __half *q, const __half *k, const __half *v, __half *o, uint32_t S, uint32_t H,
                         uint32_t dh, uint32_t ldq, uint32_t ldk, uint32_t ldv, uint32_t ldo, float scale, uint32_t B,
-                        bool *launched) {
+                        uint32_t kv_group, bool *launched) {
     *launched = false;
     if (dh != kTcDh || !aligned16((uint64_t)q) || !aligned16((uint64_t)k) || !aligned16((uint64_t)v) ||
         !aligned16((uint64_t)o) || ldq % 8 || ldk % 8 || ldv % 8 || ldo % 8 || !encode_tiled())
         return 0;   // the CUDA-core kernel handles it
-    const uint64_t cols_q = (uint64_t)H * dh;
+    const uint64_t cols_q = (uint64_t)H * dh, cols_kv = (uint64_t)(H / kv_group) * dh;
     CUtensorMap mq, mk, mv, mo;
     if (!make_map_3d(&mq, q, B, S, cols_q, ldq, (uint64_t)S * ldq, kTcRows, kTcDh) ||
-        !make_map_3d(&mk, k, B, S, cols_q, ldk, (uint64_t)S * ldk, kTcKeys, kTcDh) ||
-        !make_map_3d(&mv, v, B, S, cols_q, ldv, (uint64_t)S * ldv, kTcKeys, kTcDh) ||
+        !make_map_3d(&mk, k, B, S, cols_kv, ldk, (uint64_t)S * ldk, kTcKeys, kTcDh) ||
+        !make_map_3d(&mv, v, B, S, cols_kv, ldv, (uint64_t)S * ldv, kTcKeys, kTcDh) ||
         !make_map_3d(&mo, o, B, S, cols_q, ldo, (uint64_t)S * ldo, 32, kTcDh))
         return 0;
     static bool attr_done[kMaxDevices] = {};
@@ -607,6 +644,7 @@ int attention_tc_launch(const __half *q, const __half *k, const __half *v, __hal
     AttnArgs a;
     a.S = S;
     a.H = H;
+    a.kv_group = kv_group;
     a.nkb = (S + kTcKeys - 1) / kTcKeys;
     a.nqp = (S + 2 * kTcRows - 1) / (2 * kTcRows);
     const uint64_t items = (uint64_t)B * H * a.nqp;

@@ -74,6 +74,13 @@ SIGNATURES: dict[str, tuple] = {
     "sh_cuda_num_sms": (i32, []), "sh_cuda_timer_last_ms": (f32, []), "sh_cuda_abi_version": (u32, []),
     "sh_cuda_gemm": (i32, [u64, u64, u64, u32, u32, u32, u32, u32, u32, u64, u64, u32, u32, u32]),
     "sh_cuda_gemm_ln": (i32, [u64, u64, u64, u32, u32, u32, u32, u32, u32, u64, u64, u32, u32, u64, u64, f32, u64]),
+    "sh_rmsnorm": (None, [u64, u64, u64, u32, u32, u32, f32, u32]),
+    "sh_rope": (None, [u64, u64, u64, u32, u32, u32, u32, u32, u32]),
+    "sh_silu_mul": (None, [u64, u64, u64, u32, u32, u32, u32]),
+    "sh_softmax_masked": (None, [u64, u64, u32, u32, u32, f32, u64, u64, u32]),
+    "sh_attention_head_masked": (i32, [u64, u64, u64, u64, u32, u32, u32, u32, u32, u32, f32, u64, u32]),
+    "sh_attention_gqa": (i32, [u64, u64, u64, u64, u32, u32, u32, u32, u32, u32, u32, u32, f32, u64, u32]),
+    "sh_pixel_shuffle": (None, [u64, u64, u32, u32, u32, u32]),
     "sh_cuda_row_stats": (i32, [u64, u32, u32, u32, u64]),
     "sh_cuda_scale_rows": (i32, [u64, u64, u32, u32, u32, u32, u64]),
     "sh_cuda_add_layernorm": (None, [u64, u64, u64, u64, u64, u64, u32, u32, u32, f32]),
@@ -90,6 +97,7 @@ SIGNATURES: dict[str, tuple] = {
 EPI_ACCUMULATE, EPI_BIAS, EPI_GELU, EPI_RESIDUAL, GEMM_SIMT = 0x1, 0x2, 0x4, 0x8, 0x100
 EPI_F32_OUT, EPI_ACC_F32_IN = 0x10, 0x20
 EPI_LN_IN, EPI_STATS_OUT = 0x40, 0x80
+SH_LLM_PAD = 0xFFFF
 SH_ALL = 0xFFFFFFFF
 SH_FP16, SH_FP8, SH_INT16, SH_INT8 = 0, 1, 2, 3
 SH_XM_AUTO, SH_XM_PANEL, SH_XM_WHOLE = 0, 1, 2

@@ -89,6 +89,14 @@ class Runtime:
         self.lib.sh_cuda_synchronize()
         return self.view(addr, rows, cols, ld).cpu().numpy()
 
+    def put_bytes(self, addr: int, data: bytes) -> None:
+        """Raw bytes (e.g. a uint16 token array) to an arena address."""
+        off = addr - self.base
+        if off < 0 or off + len(data) > self.arena_bytes:
+            raise ShCudaError(f"address {addr:#x} [{len(data)} B] outside the arena")
+        src = torch.frombuffer(bytearray(data), dtype=torch.uint8)
+        self.arena[off:off + len(data)].copy_(src.to(self.arena.device))
+
     def upload(self, a: np.ndarray, align: int = 4096) -> int:
         a = np.asarray(a, dtype=np.float16)
         addr = self.alloc(*a.shape, align=align)

@@ -12,6 +12,8 @@ It imports the reference's host-side code, never this repository's oracle, and w
   siglip_s256.npz    siglip_ref.layer_reference(256, 768, 3072, 12) sampled at the frontend's dump
                      positions (64 samples per tensor) plus per-tensor float64 sums
   attention.npz      tests/gvsoc/run.py attention_reference at two shapes (inputs + output)
+  llm.npz            the decoder ops' numpy twins of frontend/smolvla_expert.py (rmsnorm, rope, silu-mul,
+                     GQA attention with a padding-token mask) and frontend/smolvla.py (rope table, pixel shuffle)
   mlir/*.mlir        frontend/siglip.emit output for the configurations the emitter tests lower
 The parity tests read only these files at run time.
 """
@@ -105,6 +107,37 @@ def main() -> None:
         att[f"{S}_{D}_{H}_k"] = lcg.fill_fp16(S, D, 22, -8, 8, 0.125).view(np.uint16)
         att[f"{S}_{D}_{H}_v"] = lcg.fill_fp16(S, D, 23, -16, 16, 0.125).view(np.uint16)
     np.savez_compressed(HERE / "attention.npz", **att)
+
+    # ---- Llama-style decoder ops (frontend/smolvla_expert.py numpy twins, frontend/smolvla.py) ---------------
+    from softhier_mlir.frontend import smolvla, smolvla_expert as ex  # noqa: E402
+    llm = {}
+    x = lcg.fill_fp16(64, 192, 31, -64, 64, 1.0 / 32)
+    g = lcg.fill_fp16(1, 192, 32, 2, 6, 0.25)
+    llm["rms_x"], llm["rms_g"] = x.view(np.uint16), g.view(np.uint16)
+    llm["rms_y"] = ex.np_rmsnorm(x, g).astype(np.float16).view(np.uint16)
+    xr = lcg.fill_fp16(16, 256, 33, -64, 64, 1.0 / 32)
+    tab = smolvla.rope_table(np.arange(16) * 3, 64).astype(np.float16)
+    llm["rope_x"], llm["rope_tab"] = xr.view(np.uint16), tab.view(np.uint16)
+    llm["rope_y"] = ex.np_rope(xr, tab, 64).astype(np.float16).view(np.uint16)
+    ga = lcg.fill_fp16(32, 128, 34, -128, 128, 1.0 / 32)
+    ub = lcg.fill_fp16(32, 128, 35, -64, 64, 1.0 / 32)
+    llm["silu_a"], llm["silu_b"] = ga.view(np.uint16), ub.view(np.uint16)
+    gf, uf = ga.astype(np.float32), ub.astype(np.float32)
+    llm["silu_y"] = ex._r16(gf / (1 + np.exp(-gf)) * uf).astype(np.float16).view(np.uint16)   # np_layer's M
+    ps = lcg.fill_fp16(64, 32, 36, -100, 100, 1.0 / 64)
+    llm["ps_x"] = ps.view(np.uint16)
+    llm["ps_y"] = smolvla.pixel_shuffle_gather(ps, 4).view(np.uint16)
+    assert np.array_equal(smolvla.pixel_shuffle(ps, 4), smolvla.pixel_shuffle_gather(ps, 4))
+    S = 64
+    q = lcg.fill_fp16(S, 3 * ex.DH, 37, -32, 32, 1.0 / 32)
+    k = lcg.fill_fp16(S, ex.DH, 38, -32, 32, 1.0 / 32)
+    v = lcg.fill_fp16(S, ex.DH, 39, -64, 64, 1.0 / 32)
+    tok = np.zeros(S, np.uint16)
+    tok[[5, 17, 40, 41, 63]] = ex.PAD_TOK
+    llm["gqa_q"], llm["gqa_k"], llm["gqa_v"], llm["gqa_tok"] = q.view(np.uint16), k.view(np.uint16), \
+        v.view(np.uint16), tok
+    llm["gqa_o"] = ex.np_attention(q, k, v, None, None, tok).astype(np.float16).view(np.uint16)
+    np.savez_compressed(HERE / "llm.npz", **llm)
 
     # ---- frontend output (dialect text the emitter must lower) ---------------------------------
     mdir = HERE / "mlir"
