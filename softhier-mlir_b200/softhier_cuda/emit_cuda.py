@@ -334,6 +334,45 @@ def _emit_ops(ops: list[D.Op], sc: Scope, defs: dict, out: list[str], tag: str, 
             rows, cols, ld, _ = sc.bufs[x].mt.geom()
             out.append(f"{ind}sh_softmax_rows({sc.haddr(op.outs[0])}, {sc.haddr(x)}, {rows}, {cols}, {ld}, "
                        f"{_f(a['scale'])}, {_cluster_c(a)});")
+        elif n == "softhier.softmax":            # token-masked (emit_c.py:363-367): the same array for rows / columns
+            x, m = op.operands[:2]
+            rows, cols, ld, _ = sc.bufs[x].mt.geom()
+            out.append(f"{ind}sh_softmax_masked({sc.haddr(op.outs[0])}, {sc.haddr(x)}, {rows}, {cols}, {ld}, "
+                       f"{_f(a['scale'])}, {sc.haddr(m)}, {sc.haddr(m)}, {_cluster_c(a)});")
+        elif n == "softhier.rmsnorm":
+            x, g = op.operands[:2]
+            rows, cols, ld, _ = sc.bufs[x].mt.geom()
+            out.append(f"{ind}sh_rmsnorm({sc.haddr(op.outs[0])}, {sc.haddr(x)}, {sc.haddr(g)}, {rows}, {cols}, {ld}, "
+                       f"{_f(a['eps'])}, {_cluster_c(a)});")
+        elif n == "softhier.rope":
+            x, t = op.operands[:2]
+            rows, cols, ld, _ = sc.bufs[x].mt.geom()
+            ldt = sc.bufs[t].mt.geom()[2]
+            out.append(f"{ind}sh_rope({sc.haddr(op.outs[0])}, {sc.haddr(x)}, {sc.haddr(t)}, {rows}, {cols}, {ld}, {ldt}, "
+                       f"{int(a['head_dim'])}, {_cluster_c(a)});")
+        elif n == "softhier.silu_mul" and len(op.operands) == 2 and \
+                sc.bufs[op.operands[0]].mt.geom()[2] == sc.bufs[op.operands[1]].mt.geom()[2] == \
+                sc.bufs[op.outs[0]].mt.geom()[2]:   # one leading dimension (emit_c.py:381-385)
+            x, y = op.operands
+            rows, cols, ld, _ = sc.bufs[x].mt.geom()
+            out.append(f"{ind}sh_silu_mul({sc.haddr(op.outs[0])}, {sc.haddr(x)}, {sc.haddr(y)}, {rows}, {cols}, {ld}, "
+                       f"{_cluster_c(a)});")
+        elif n == "softhier.pixel_shuffle":
+            src = op.operands[0]
+            rows, cols, _, _ = sc.bufs[src].mt.geom()
+            grid = int(round(rows ** 0.5))
+            out.append(f"{ind}sh_pixel_shuffle({sc.haddr(op.outs[0])}, {sc.haddr(src)}, {grid}, {cols}, "
+                       f"{int(a['scale'])}, {_cluster_c(a)});")
+        elif n == "softhier.attention" and (len(op.operands) == 4 or "kv_heads" in a):
+            q, k, v = op.operands[:3]
+            o = op.outs[0]
+            S, Dm, ldq, _ = sc.bufs[q].mt.geom()
+            ldk, ldv, ldo = (sc.bufs[t].mt.geom()[2] for t in (k, v, o))
+            H = int(a["heads"])
+            hkv = int(a.get("kv_heads", H))
+            m = sc.haddr(op.operands[3]) if len(op.operands) == 4 else "0"
+            out.append(f"{ind}sh_attention_gqa({sc.haddr(q)}, {sc.haddr(k)}, {sc.haddr(v)}, {sc.haddr(o)}, {S}, {Dm}, "
+                       f"{H}, {hkv}, {ldq}, {ldk}, {ldv}, {ldo}, {_f(a['scale'])}, {m}, {_cluster_c(a)});")
         elif n == "softhier.scale":
             x = op.operands[0]
             rows, cols, ld, _ = sc.bufs[x].mt.geom()
@@ -544,6 +583,39 @@ class Program:
             rows, cols, ld, _ = mx.geom()
             lib.sh_softmax_rows(y, x, rows, cols, ld, a["scale"], _cluster_v(a))
             return 0
+        if n == "softhier.softmax":
+            (x, mx), (m, _), (y, _) = A(op.operands[0]), A(op.operands[1]), A(op.outs[0])
+            rows, cols, ld, _ = mx.geom()
+            lib.sh_softmax_masked(y, x, rows, cols, ld, a["scale"], m, m, _cluster_v(a))
+            return 0
+        if n == "softhier.rmsnorm":
+            (x, mx), (g, _), (y, _) = A(op.operands[0]), A(op.operands[1]), A(op.outs[0])
+            rows, cols, ld, _ = mx.geom()
+            lib.sh_rmsnorm(y, x, g, rows, cols, ld, a["eps"], _cluster_v(a))
+            return 0
+        if n == "softhier.rope":
+            (x, mx), (t, mt), (y, _) = A(op.operands[0]), A(op.operands[1]), A(op.outs[0])
+            rows, cols, ld, _ = mx.geom()
+            lib.sh_rope(y, x, t, rows, cols, ld, mt.geom()[2], int(a["head_dim"]), _cluster_v(a))
+            return 0
+        if n == "softhier.silu_mul" and len(op.operands) == 2:
+            (x, mx), (b, mb), (y, my) = A(op.operands[0]), A(op.operands[1]), A(op.outs[0])
+            rows, cols, ld, _ = mx.geom()
+            if mb.geom()[2] == ld == my.geom()[2]:
+                lib.sh_silu_mul(y, x, b, rows, cols, ld, _cluster_v(a))
+                return 0
+        if n == "softhier.pixel_shuffle":
+            (x, mx), (y, _) = A(op.operands[0]), A(op.outs[0])
+            rows, cols, _, _ = mx.geom()
+            lib.sh_pixel_shuffle(y, x, int(round(rows ** 0.5)), cols, int(a["scale"]), _cluster_v(a))
+            return 0
+        if n == "softhier.attention" and (len(op.operands) == 4 or "kv_heads" in a):
+            (q, mq), (k, mk), (v, mv), (o, mo) = (A(t) for t in (*op.operands[:3], op.outs[0]))
+            S, Dm, ldq, _ = mq.geom()
+            H = int(a["heads"])
+            m = A(op.operands[3])[0] if len(op.operands) == 4 else 0
+            return lib.sh_attention_gqa(q, k, v, o, S, Dm, H, int(a.get("kv_heads", H)), ldq, mk.geom()[2],
+                                        mv.geom()[2], mo.geom()[2], a["scale"], m, _cluster_v(a))
         if n in ("softhier.gelu", "softhier.scale"):
             (x, mx), (y, _) = A(op.operands[0]), A(op.outs[0])
             rows, cols, ld, _ = mx.geom()

@@ -18,9 +18,10 @@ ROOT = Path(__file__).resolve().parents[1]
 REF = Path(os.environ.get("SOFTHIER_REF", "/root/reference"))
 FC = REF / "tests" / "filecheck"
 MLIR = Path(__file__).resolve().parent / "golden" / "mlir"
-# translate tests on the operator-library path (the others exercise TCDM / LLM / training ops outside it)
+# translate tests of the operator library and the decoder ops (the others exercise TCDM / expert / training ops)
 HOT_TRANSLATE = ["gemm512_translate.mlir", "gemm_nonconst_translate.mlir", "hbm_ops_translate.mlir",
-                 "attention_translate.mlir", "loop_translate.mlir", "mark_translate.mlir", "gemm_xmcast_translate.mlir"]
+                 "attention_translate.mlir", "loop_translate.mlir", "mark_translate.mlir", "gemm_xmcast_translate.mlir",
+                 "llm_translate.mlir"]
 OPT = ["distribute_summa.mlir", "pipeline_gemm.mlir", "linalg_gemm512.mlir"]
 needs_ref = pytest.mark.skipif(not FC.exists(), reason="reference checkout not present")
 

@@ -132,3 +132,52 @@ def test_llm_errors(gpu_lib, capfd):
     assert "[sh_rope]" in cap.out + cap.err
     assert lib.sh_cuda_last_error() == -1
     rt.check()
+
+
+DECODER = """builtin.module {
+  func.func @dec() {
+    %x   = softhier.hbm_buffer {offset = 65536 : i32}  : memref<128x192xf16, "hbm_west">
+    %g   = softhier.hbm_buffer {offset = 131072 : i32} : memref<1x192xf16, "hbm_west">
+    %ln  = softhier.hbm_buffer {offset = 139264 : i32} : memref<128x192xf16, "hbm_west">
+    %tab = softhier.hbm_buffer {offset = 196608 : i32} : memref<128x64xf16, "hbm_west">
+    %tok = softhier.hbm_buffer {offset = 229376 : i32} : memref<128xi16, "hbm_west">
+    %kv  = softhier.hbm_buffer {offset = 233472 : i32} : memref<128x128xf16, "hbm_west">
+    %o   = softhier.hbm_buffer {offset = 270336 : i32} : memref<128x192xf16, "hbm_west">
+    %m   = softhier.hbm_buffer {offset = 327680 : i32} : memref<128x192xf16, "hbm_west">
+    %k = softhier.view %kv : memref<128x128xf16, "hbm_west"> -> memref<128x64xf16, strided<[128, 1], offset: 0>, "hbm_west">
+    %v = softhier.view %kv : memref<128x128xf16, "hbm_west"> -> memref<128x64xf16, strided<[128, 1], offset: 64>, "hbm_west">
+    softhier.hbm_fill_lcg %x {seed = 71 : i32, lo = -64 : i32, hi = 64 : i32, scale = 0.03125 : f32} : memref<128x192xf16, "hbm_west">
+    softhier.hbm_fill_lcg %g {seed = 72 : i32, lo = 2 : i32, hi = 6 : i32, scale = 0.25 : f32} : memref<1x192xf16, "hbm_west">
+    softhier.hbm_fill_lcg %tab {seed = 73 : i32, lo = -32 : i32, hi = 32 : i32, scale = 0.03125 : f32} : memref<128x64xf16, "hbm_west">
+    softhier.hbm_fill_lcg %kv {seed = 74 : i32, lo = -32 : i32, hi = 32 : i32, scale = 0.03125 : f32} : memref<128x128xf16, "hbm_west">
+    softhier.rmsnorm %x, %g -> %ln {eps = 1.0e-5 : f32, cluster = -1 : i32} : memref<128x192xf16, "hbm_west">, memref<1x192xf16, "hbm_west"> -> memref<128x192xf16, "hbm_west">
+    softhier.rope %ln, %tab -> %ln {head_dim = 64 : i32, cluster = -1 : i32} : memref<128x192xf16, "hbm_west">, memref<128x64xf16, "hbm_west"> -> memref<128x192xf16, "hbm_west">
+    softhier.attention %ln, %k, %v, %tok -> %o {scale = 0.125 : f32, heads = 3 : i32, kv_heads = 1 : i32, cluster = -1 : i32}
+        : memref<128x192xf16, "hbm_west">, memref<128x64xf16, strided<[128, 1], offset: 0>, "hbm_west">, memref<128x64xf16, strided<[128, 1], offset: 64>, "hbm_west">, memref<128xi16, "hbm_west"> -> memref<128x192xf16, "hbm_west">
+    softhier.silu_mul %o, %x -> %m {cluster = -1 : i32} : memref<128x192xf16, "hbm_west">, memref<128x192xf16, "hbm_west"> -> memref<128x192xf16, "hbm_west">
+    func.return
+  }
+}
+"""
+
+
+def test_decoder_module_through_emit_cuda(gpu_lib, capfd):
+    """A decoder block in the dialect (rmsnorm -> rope -> masked GQA attention on a strided K|V buffer -> silu-mul),
+    lowered by emit_cuda and run in-process, against the oracle chain."""
+    from softhier_cuda import emit_cuda as E
+    rt = gpu_lib
+    rt.reset()
+    prog = E.Program(DECODER, rt)
+    assert prog.run_phase("prologue") == 0
+    tok = (np.arange(128) // 16).astype(np.uint16)
+    tok[[9, 100]] = llm.PAD
+    rt.put_bytes(prog.address("tok")[0], tok.tobytes())
+    assert prog.run_phase("kernel") == 0
+    rt.check()
+    x, g, tab, kv = (prog.tensor(n).astype(np.float32) for n in ("x", "g", "tab", "kv"))
+    ln = llm.rope(llm.rmsnorm(x, g), tab, 64)
+    o = llm.attention_gqa(ln, kv[:, :64], kv[:, 64:], 3, 1, 0.125, tok, rounding=False)
+    want = llm.silu_mul(llm.r16(o), x, rounding=False)
+    got = prog.tensor("m").astype(np.float32)
+    err, rel = ops.max_abs_and_rel_l2(got, want)
+    assert err <= 2e-2 and rel <= 5e-3, (err, rel)
