@@ -115,6 +115,17 @@ void sh_cuda_fill_normal_fp16(uint64_t a, uint32_t rows, uint32_t cols, uint32_t
 void sh_cuda_fill_lcg_block(uint64_t a, uint32_t rows, uint32_t cols, uint32_t ld, uint32_t seed, int lo, int hi,
                             float scale, uint64_t row0, uint64_t col0, uint64_t gcols);
 
+/* ---- HBM preload images -------------------------------------------------------------------------------------------
+ * No counterpart in the reference's C runtime (its simulator loads the image at reset): the ELF32 images of
+ * softhier_mlir/sim/preload.py (one PT_LOAD segment per array, physical address hbm_base + HBM offset, hbm_base
+ * 0xC0000000 there) copied into the arena at sh_hbm_addr(offset) with synchronous copies; bytes between a
+ * segment's file size and memory size are zeroed. Returns the number of segments, -1 (bad file) or -2 (a segment
+ * outside the arena). sh_preload_elf_segments only lists the segments (offsets, memory sizes; no GPU needed) and
+ * returns their count. */
+int sh_cuda_preload_elf(const char *path, uint64_t hbm_base);
+int sh_preload_elf_segments(const char *path, uint64_t hbm_base, uint64_t *offsets, uint64_t *sizes,
+                            uint32_t max_segments);
+
 /* ---- peer memory for the multi-GPU SUMMA --------------------------------------------------------------------------
  * Device buffers that other processes of the node can map (CUDA IPC), and asynchronous 2-D copies between any two
  * device addresses of the node (copy engines over NVLink when source and destination are on different GPUs). */

@@ -7,6 +7,7 @@
 #include <time.h>
 
 #include <mutex>
+#include <vector>
 
 #include "sh_internal.cuh"
 
@@ -277,6 +278,105 @@ uint32_t sh_l1_size(void) { return (uint32_t)state().smem_optin; }
 void sh_preload_wait(uint64_t) { sh_barrier_global(); }
 void sh_call_on_core_stack(void (*fn)(void), uint32_t) {
     if (fn) fn();
+}
+
+// ---- HBM preload images ---------------------------------------------------------------------------------------
+// The reference's preload image (softhier_mlir/sim/preload.py: make_preload_elf) is an ELF32 little-endian file
+// whose PT_LOAD segments carry raw array bytes at physical address hbm_base + HBM byte offset; GVSoC's loader writes
+// them into HBM at reset. Here the same image is copied into the arena (sh_hbm_addr(offset)) with synchronous host
+// copies, so the sentinel it ends with is visible as soon as sh_cuda_preload_elf returns.
+
+}  // extern "C"
+
+namespace {
+
+struct Segment {
+    uint64_t offset, file_off, filesz, memsz;
+};
+
+uint32_t rd32(const unsigned char *p) { return p[0] | (p[1] << 8) | (p[2] << 16) | ((uint32_t)p[3] << 24); }
+uint16_t rd16(const unsigned char *p) { return (uint16_t)(p[0] | (p[1] << 8)); }
+
+// Reads the file and lists its PT_LOAD segments; false (reason recorded) on anything that is not such an image.
+bool parse_preload(const char *path, uint64_t hbm_base, const char *who, std::vector<unsigned char> &data,
+                   std::vector<Segment> &segs) {
+    FILE *f = path ? fopen(path, "rb") : nullptr;
+    if (!f) {
+        sh::set_error(-1, "[%s] cannot open %s", who, path ? path : "(null)");
+        return false;
+    }
+    fseek(f, 0, SEEK_END);
+    const long n = ftell(f);
+    fseek(f, 0, SEEK_SET);
+    data.resize(n > 0 ? (size_t)n : 0);
+    const size_t got = n > 0 ? fread(data.data(), 1, (size_t)n, f) : 0;
+    fclose(f);
+    const unsigned char *d = data.data();
+    if (got != data.size() || data.size() < 52 || memcmp(d, "\x7f" "ELF", 4) != 0 || d[4] != 1 || d[5] != 1) {
+        sh::set_error(-1, "[%s] %s is not a little-endian ELF32 image", who, path);
+        return false;
+    }
+    const uint32_t phoff = rd32(d + 28);
+    const uint16_t phentsize = rd16(d + 42), phnum = rd16(d + 44);
+    if (phentsize < 32 || (uint64_t)phoff + (uint64_t)phnum * phentsize > data.size()) {
+        sh::set_error(-1, "[%s] %s: program headers out of the file", who, path);
+        return false;
+    }
+    segs.clear();
+    for (uint32_t i = 0; i < phnum; ++i) {
+        const unsigned char *ph = d + phoff + (size_t)i * phentsize;
+        if (rd32(ph) != 1) continue;   // PT_LOAD only
+        const uint64_t fo = rd32(ph + 4), paddr = rd32(ph + 12), fsz = rd32(ph + 16), msz = rd32(ph + 20);
+        if (paddr < hbm_base || fo + fsz > data.size() || msz < fsz) {
+            sh::set_error(-1, "[%s] %s: segment %u (paddr %#llx, %llu B at file offset %llu) is malformed", who, path,
+                          i, (unsigned long long)paddr, (unsigned long long)fsz, (unsigned long long)fo);
+            return false;
+        }
+        segs.push_back(Segment{paddr - hbm_base, fo, fsz, msz});
+    }
+    return true;
+}
+
+}  // namespace
+
+extern "C" {
+
+int sh_preload_elf_segments(const char *path, uint64_t hbm_base, uint64_t *offsets, uint64_t *sizes,
+                            uint32_t max_segments) {
+    std::vector<unsigned char> data;
+    std::vector<Segment> segs;
+    if (!parse_preload(path, hbm_base, "sh_preload_elf_segments", data, segs)) return -1;
+    for (size_t i = 0; i < segs.size() && i < max_segments; ++i) {
+        if (offsets) offsets[i] = segs[i].offset;
+        if (sizes) sizes[i] = segs[i].memsz;
+    }
+    return (int)segs.size();
+}
+
+int sh_cuda_preload_elf(const char *path, uint64_t hbm_base) {
+    std::vector<unsigned char> data;
+    std::vector<Segment> segs;
+    if (!parse_preload(path, hbm_base, "sh_cuda_preload_elf", data, segs)) return -1;
+    DeviceState &s = state();
+    if (!s.arena) {
+        set_error(-1, "[sh_cuda_preload_elf] no arena bound (sh_init or sh_cuda_set_arena first)");
+        return -1;
+    }
+    for (const Segment &g : segs)
+        if (g.offset + g.memsz > s.arena_bytes) {
+            set_error(-2, "[sh_cuda_preload_elf] segment at %#llx (%llu B) is outside the %zu B arena",
+                      (unsigned long long)g.offset, (unsigned long long)g.memsz, s.arena_bytes);
+            return -2;
+        }
+    for (const Segment &g : segs) {
+        if (g.filesz && !cuda_ok(cudaMemcpy(s.arena + g.offset, data.data() + g.file_off, g.filesz,
+                                            cudaMemcpyHostToDevice), "sh_cuda_preload_elf"))
+            return -1;
+        if (g.memsz > g.filesz &&
+            !cuda_ok(cudaMemset(s.arena + g.offset + g.filesz, 0, g.memsz - g.filesz), "sh_cuda_preload_elf"))
+            return -1;
+    }
+    return (int)segs.size();
 }
 
 // ---- sh_ops_cuda.h ------------------------------------------------------------------------------------------

@@ -81,6 +81,8 @@ SIGNATURES: dict[str, tuple] = {
     "sh_attention_head_masked": (i32, [u64, u64, u64, u64, u32, u32, u32, u32, u32, u32, f32, u64, u32]),
     "sh_attention_gqa": (i32, [u64, u64, u64, u64, u32, u32, u32, u32, u32, u32, u32, u32, f32, u64, u32]),
     "sh_pixel_shuffle": (None, [u64, u64, u32, u32, u32, u32]),
+    "sh_cuda_preload_elf": (i32, [cp, u64]),
+    "sh_preload_elf_segments": (i32, [cp, u64, C.c_void_p, C.c_void_p, u32]),
     "sh_cuda_row_stats": (i32, [u64, u32, u32, u32, u64]),
     "sh_cuda_scale_rows": (i32, [u64, u64, u32, u32, u32, u32, u64]),
     "sh_cuda_add_layernorm": (None, [u64, u64, u64, u64, u64, u64, u32, u32, u32, f32]),

@@ -12,6 +12,8 @@ It imports the reference's host-side code, never this repository's oracle, and w
   siglip_s256.npz    siglip_ref.layer_reference(256, 768, 3072, 12) sampled at the frontend's dump
                      positions (64 samples per tensor) plus per-tensor float64 sums
   attention.npz      tests/gvsoc/run.py attention_reference at two shapes (inputs + output)
+  preload_small.elf  a small HBM preload image written by sim/preload.make_preload_elf (3 arrays + sentinel),
+  preload_small.npz  its segments as sim/preload.read_preload_elf returns them
   llm.npz            the decoder ops' numpy twins of frontend/smolvla_expert.py (rmsnorm, rope, silu-mul,
                      GQA attention with a padding-token mask) and frontend/smolvla.py (rope table, pixel shuffle)
   mlir/*.mlir        frontend/siglip.emit output for the configurations the emitter tests lower
@@ -138,6 +140,17 @@ def main() -> None:
         v.view(np.uint16), tok
     llm["gqa_o"] = ex.np_attention(q, k, v, None, None, tok).astype(np.float16).view(np.uint16)
     np.savez_compressed(HERE / "llm.npz", **llm)
+
+    # ---- HBM preload image (softhier_mlir/sim/preload.py) ----------------------------------------------------
+    from softhier_mlir.sim import preload  # noqa: E402
+    arrays = {0x1000: lcg.fill_fp16(16, 32, 41, -100, 100, 1.0 / 64),
+              0x2040: np.arange(100, dtype=np.uint8),
+              0x3000: lcg.fill_fp16(8, 64, 42, -8, 8, 0.125)}
+    arrays[0x4000] = preload.sentinel_array()
+    preload.make_preload_elf(HERE / "preload_small.elf", arrays)
+    seg = preload.read_preload_elf(HERE / "preload_small.elf")
+    np.savez_compressed(HERE / "preload_small.npz", offsets=np.array(sorted(seg), np.uint64),
+                        **{f"seg_{off:x}": np.frombuffer(seg[off], np.uint8) for off in seg})
 
     # ---- frontend output (dialect text the emitter must lower) ---------------------------------
     mdir = HERE / "mlir"

@@ -65,3 +65,22 @@ def test_check_gemm_helper(gpu_lib, capfd):
     bad = lib.sh_test_check_gemm(x, w, z, M, N, K, K, N, N, 128, 0.5, 0.0, b"[gemm]")
     assert bad == 0
     assert "[gemm] samples=128 bad=0" in capfd.readouterr().out
+
+
+def test_preload_elf_into_arena(gpu_lib):
+    """An image written by the reference's sim/preload.make_preload_elf lands at sh_hbm_addr(offset)."""
+    from pathlib import Path
+    import numpy as np
+    from conftest import golden
+    rt, lib = gpu_lib, gpu_lib.lib
+    rt.reset()
+    rt.arena.zero_()
+    g = golden("preload_small.npz")
+    path = Path(__file__).resolve().parent / "golden" / "preload_small.elf"
+    assert lib.sh_cuda_preload_elf(str(path).encode(), 0xC0000000) == len(g["offsets"])
+    for off in g["offsets"]:
+        seg = g[f"seg_{int(off):x}"]
+        got = rt.arena[int(off):int(off) + len(seg)].cpu().numpy()
+        np.testing.assert_array_equal(got, seg)
+    lib.sh_preload_wait(lib.sh_hbm_addr(int(g["offsets"][-1])))
+    rt.check()
