@@ -718,7 +718,7 @@ def run_summa(args, rank: int, world: int, local: int) -> dict | None:
     su = SU.SummaGPU(rt.lib, lay, rank, exchange, bar, (compute, copy))
     su.fill_inputs(41, 42)
     for _ in range(max(3, args.warmup)):
-        assert su.step(torch) == 0
+        assert su.step(torch, prefetch_next=True) == 0
     torch.cuda.synchronize()
     rt.check()
     clocks = ClockSampler(local)
@@ -729,8 +729,9 @@ def run_summa(args, rank: int, world: int, local: int) -> dict | None:
     time.sleep(0.05)
     steps = args.steps
     e0.record(compute)
-    for _ in range(steps):
-        su.step(torch)
+    for _ in range(steps):         # each step also pulls the next step's first panel (the last one's ends in e1)
+        su.step(torch, prefetch_next=True)
+    su.finish(torch)
     e1.record(compute)
     e1.synchronize()
     clock_info = clocks.stop()

@@ -153,13 +153,20 @@ class SummaGPU:
         lib.sh_cuda_synchronize()
         self.barrier()        # every block exists before any rank pulls from it
 
-    def step(self, torch) -> int:
-        """C_ij = sum over panels (enqueued; returns 0 or the first failing return code)."""
+    def step(self, torch, prefetch_next: bool = False) -> int:
+        """C_ij = sum over panels (enqueued; returns 0 or the first failing return code). With prefetch_next the
+        first panel of the next step (the same panels: inputs are read-only) is pulled while this step's last GEMM
+        runs, so that a run of steps keeps the copy engines busy across step boundaries."""
         lay, lib = self.lay, self.lib
         lib.sh_cuda_set_stream(self.compute.cuda_stream)
-        copy_done = [torch.cuda.Event(), torch.cuda.Event()]
-        gemm_done = [torch.cuda.Event(), torch.cuda.Event()]
+        if not hasattr(self, "_ev"):
+            self._ev = {"copy": [torch.cuda.Event(), torch.cuda.Event()],
+                        "gemm": [torch.cuda.Event(), torch.cuda.Event()]}
+            self._gemm_recorded = [False, False]
+            self._prefetched = False
+        copy_done, gemm_done = self._ev["copy"], self._ev["gemm"]
         pulled = [False, False]
+        n = len(self.sched)
 
         def pull(idx: int):
             p, s = self.sched[idx], idx % 2
@@ -167,8 +174,8 @@ class SummaGPU:
             if p.a_rank == self.rank and p.b_rank == self.rank:
                 return
             with torch.cuda.stream(self.copy):
-                if idx >= 2:
-                    self.copy.wait_event(gemm_done[s])       # the GEMM that read this slot is done
+                if self._gemm_recorded[s]:
+                    self.copy.wait_event(gemm_done[s])       # the last GEMM that read this slot is done
                 if p.a_rank != self.rank:
                     lib.sh_cuda_copy2d(self.a_pan[s], lay.kb * 2, self.peer_a[p.a_rank] + 2 * p.a_col, lay.Kc * 2,
                                        lay.kb * 2, lay.Mb, self.copy.cuda_stream)
@@ -178,13 +185,21 @@ class SummaGPU:
                 copy_done[s].record(self.copy)
             pulled[s] = True
 
-        self.copy.wait_stream(self.compute)   # the previous step's GEMMs are done with both panel slots
-        pull(0)
+        if self._prefetched:                      # panel 0 is already on its way (previous step's prefetch)
+            p0 = self.sched[0]
+            pulled[0] = not (p0.a_rank == self.rank and p0.b_rank == self.rank)
+            self._prefetched = False
+        else:
+            pull(0)
         rc = 0
         for idx, p in enumerate(self.sched):
             s = idx % 2
-            if idx + 1 < len(self.sched):
+            if idx + 1 < n:
                 pull(idx + 1)
+            elif prefetch_next and n % 2 == 0 and n > 1:
+                # the next step's panel 0 goes to slot 0, last read by this step's panel n - 2
+                pull(0)
+                self._prefetched = True
             with torch.cuda.stream(self.compute):
                 if pulled[s]:
                     self.compute.wait_event(copy_done[s])
@@ -196,7 +211,7 @@ class SummaGPU:
                     b, ldb = self.b_loc + 2 * p.b_row * lay.Nb, lay.Nb
                 else:
                     b, ldb = self.b_pan[s], lay.Nb
-                last = idx == len(self.sched) - 1
+                last = idx == n - 1
                 if self.acc is None:            # one panel: straight to fp16
                     z, flags, res = self.c, 0, 0
                 elif idx == 0:
@@ -207,7 +222,13 @@ class SummaGPU:
                     z, flags, res = self.c, L.EPI_ACC_F32_IN, self.acc
                 rc = rc or lib.sh_cuda_gemm(a, b, z, lay.Mb, lay.Nb, lay.kb, lda, ldb, lay.Nb, 0, res, lay.Nb, flags, 1)
                 gemm_done[s].record(self.compute)
+                self._gemm_recorded[s] = True
         return rc
+
+    def finish(self, torch) -> None:
+        """Make the compute stream wait for an outstanding prefetch (so a timed region ends after it)."""
+        if getattr(self, "_prefetched", False):
+            self.compute.wait_stream(self.copy)
 
     def close(self):
         for p in self.opened:

@@ -37,8 +37,11 @@ def main():
 
         su = SU.SummaGPU(rt.lib, lay, rank, exchange, dist.barrier, (torch.cuda.Stream(), torch.cuda.Stream()))
         su.fill_inputs(31, 32)
-        for _ in range(2):                       # two steps: the second reuses the panel slots
-            assert su.step(torch) == 0
+        # three steps: the second reuses the panel slots, and the first two pull the next step's first panel
+        # early (prefetch_next), so the last one runs on a prefetched panel 0
+        for k in range(3):
+            assert su.step(torch, prefetch_next=k < 2) == 0
+        su.finish(torch)
         torch.cuda.synchronize()
         rt.check()
         i, j = lay.coords(rank)
