@@ -70,8 +70,6 @@ bool make_map_2d_sw(CUtensorMap *m, const void *base, uint64_t rows, uint64_t co
                     uint32_t box_cols, CUtensorMapSwizzle sw);
 // 3-D fp16 tensor [batches, rows, cols]: row stride ld elements, batch stride batch_ld elements, box
 // [1, box_rows, box_cols], 128-byte swizzle. Rows past `rows` inside a batch read as zeros.
-bool make_map_3d_sw(CUtensorMap *m, const void *base, uint64_t batches, uint64_t rows, uint64_t cols, uint64_t ld,
-                    uint64_t batch_ld, uint32_t box_rows, uint32_t box_cols, CUtensorMapSwizzle sw);
 bool make_map_3d(CUtensorMap *m, const void *base, uint64_t batches, uint64_t rows, uint64_t cols, uint64_t ld,
                  uint64_t batch_ld, uint32_t box_rows, uint32_t box_cols);
 

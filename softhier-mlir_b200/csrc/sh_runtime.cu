@@ -180,19 +180,6 @@ bool make_map_2d_sw(CUtensorMap *m, const void *base, uint64_t rows, uint64_t co
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-bool make_map_3d_sw(CUtensorMap *m, const void *base, uint64_t batches, uint64_t rows, uint64_t cols, uint64_t ld,
-                    uint64_t batch_ld, uint32_t box_rows, uint32_t box_cols, CUtensorMapSwizzle sw) {
-    PFN_encodeTiled enc = encode_tiled();
-    if (!enc) return false;
-    cuuint64_t dims[3] = {cols, rows, batches};
-    cuuint64_t strides[2] = {ld * 2, batch_ld * 2};
-    cuuint32_t box[3] = {box_cols, box_rows, 1};
-    cuuint32_t estr[3] = {1, 1, 1};
-    return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void *>(base), dims, strides, box, estr,
-               CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
 bool make_map_3d(CUtensorMap *m, const void *base, uint64_t batches, uint64_t rows, uint64_t cols, uint64_t ld,
                  uint64_t batch_ld, uint32_t box_rows, uint32_t box_cols) {
     PFN_encodeTiled enc = encode_tiled();
