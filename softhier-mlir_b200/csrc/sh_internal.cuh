@@ -137,6 +137,12 @@ __device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t *p, uint32_t v
     return old;
 }
 
+// Programmatic dependent launch: a kernel launched with cudaLaunchAttributeProgrammaticStreamSerialization may
+// start while its stream predecessor still runs; pdl_wait() blocks until that predecessor has completed and its
+// memory is visible, so everything before it must touch no memory a predecessor writes or reads.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // Bounded wait that ignores the abort flag: used to drain outstanding asynchronous work before exit.
 __device__ __forceinline__ void drain_wait(uint64_t *bar, uint32_t parity) {
     const long long t0 = clock64();
