@@ -547,11 +547,36 @@ def run_gemm(args, local: int) -> dict:
     flop = 2.0 * M * N * K
     pk, src = peaks()
     tf = flop / ms / 1e9
-    return {"metric": "GEMM TFLOP/s", "value": round(tf, 1), "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "dtype": "f16",
-            "frac_of_peak": round(tf / pk["bf16_tflops"], 4), "peak": f"{src} bf16 burst {pk['bf16_tflops']} TFLOP/s",
-            "config": {"workload": f"sh_cuda_gemm {M}x{N}x{K} epilogue [{args.epi}]",
-                       "l2": "Z alone larger than L2 at the default shape; no flush"}}
+    out = {"metric": "GEMM TFLOP/s", "value": round(tf, 1), "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps,
+           "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "dtype": "f16",
+           "frac_of_peak": round(tf / pk["bf16_tflops"], 4), "peak": f"{src} bf16 burst {pk['bf16_tflops']} TFLOP/s",
+           "config": {"workload": f"sh_cuda_gemm {M}x{N}x{K} epilogue [{args.epi}]",
+                      "l2": "Z alone larger than L2 at the default shape; no flush"}}
+    if args.vs_cublas:
+        out["vs_cublas"] = _vs_cublas(torch, stream, call, M, N, K, max(1, args.steps))
+        rt.check()
+    return out
+
+
+def _vs_cublas(torch, stream, call, M: int, N: int, K: int, steps: int, reps: int = 3) -> dict:
+    """Library comparison on the same shape: torch.matmul (cuBLAS) fp16 with the same operand distributions,
+    timed the same way, alternating with this library's call so both see the same clocks. cuBLAS has no fused
+    epilogue: compare against `--epi ""`."""
+    a = torch.randn(M, K, device=stream.device, dtype=torch.float16)
+    b = torch.randn(K, N, device=stream.device, dtype=torch.float16) * 0.02
+    c = torch.empty(M, N, device=stream.device, dtype=torch.float16)
+    cub = lambda: torch.matmul(a, b, out=c)  # noqa: E731
+    ours, theirs = [], []
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            cub()
+        for _ in range(reps):
+            ours.append(_event_time(torch, stream, call, steps))
+            theirs.append(_event_time(torch, stream, cub, steps))
+    flop = 2.0 * M * N * K
+    med = lambda v: sorted(v)[len(v) // 2]  # noqa: E731
+    return {"ours_tflops": round(flop / med(ours) / 1e9, 1), "cublas_tflops": round(flop / med(theirs) / 1e9, 1),
+            "ratio": round(med(theirs) / med(ours), 3), "reps": reps, "statistic": "median of alternating reps"}
 
 
 def run_attention(args, local: int) -> dict:
@@ -775,6 +800,7 @@ def main():
     ap.add_argument("--gemm", default="131072,3072,768", help="M,N,K of --workload gemm")
     ap.add_argument("--epi", default="bias,gelu", help="fused epilogue of --workload gemm: bias,gelu,residual")
     ap.add_argument("--summa-n", type=int, default=16384)
+    ap.add_argument("--vs-cublas", action="store_true", help="--workload gemm: also time torch.matmul on the shape")
     args = ap.parse_args()
     rank, world, local = dist_env()
     if args.impl == "reference":

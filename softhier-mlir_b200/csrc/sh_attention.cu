@@ -36,6 +36,8 @@ __global__ void __launch_bounds__(kSimtRows) k_attn_simt(const __half *q, const 
     __shared__ float ks[kSimtKeys][DH];
     __shared__ float vs[kSimtKeys][DH];
     __shared__ uint16_t ts[kSimtKeys];
+    pdl_launch_dependents();
+    pdl_wait();
     const uint32_t b = blockIdx.z, h = blockIdx.y;
     const uint32_t row = blockIdx.x * kSimtRows + threadIdx.x;
     const size_t r0 = (size_t)b * S;
@@ -130,9 +132,8 @@ int run(uint64_t q, uint64_t k, uint64_t v, uint64_t o, uint32_t S, uint32_t H, 
     }
     cudaStream_t st = sh::stream();
 #define SH_ATTN_SIMT(DHT)                                                                                        \
-    k_attn_simt<DHT><<<grid, kSimtRows, 0, st>>>((const __half *)q, (const __half *)k, (const __half *)v,        \
-                                                 (__half *)o, S, dh, ldq, ldk, ldv, ldo, sl2, kv_group,          \
-                                                 (const uint16_t *)tok)
+    sh::launch_pdl(k_attn_simt<DHT>, grid, dim3(kSimtRows), 0, st, (const __half *)q, (const __half *)k,      \
+                   (const __half *)v, (__half *)o, S, dh, ldq, ldk, ldv, ldo, sl2, kv_group, (const uint16_t *)tok)
     if (dh <= 16)
         SH_ATTN_SIMT(16);
     else if (dh <= 32)
@@ -325,6 +326,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    // set-up above overlaps the previous kernel (programmatic dependent launch); Q/K/V only after it is done
+    pdl_launch_dependents();
+    pdl_wait();
 
     if (warp == 0) {
         if (lane == 0) {
@@ -653,8 +657,10 @@ int attention_tc_launch(const __half *q, const __half *k, const __half *v, __hal
     a.sl2 = scale * 1.4426950408889634f;
     a.err = state().dev_err;
     const uint32_t grid = (uint32_t)std::min<uint64_t>(items, (uint64_t)state().num_sms);
-    k_attn_tc<<<grid, kAttnThreads, kAttnSmem, stream()>>>(mq, mk, mv, mo, a);
     *launched = true;
-    return cuda_ok(cudaGetLastError(), "sh_attention") ? 0 : -1;
+    return cuda_ok(launch_pdl(k_attn_tc, dim3(grid), dim3(kAttnThreads), kAttnSmem, stream(), mq, mk, mv, mo, a),
+                   "sh_attention")
+               ? 0
+               : -1;
 }
 }  // namespace sh

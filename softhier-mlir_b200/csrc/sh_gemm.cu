@@ -820,28 +820,6 @@ __global__ void __launch_bounds__(256) k_gemm_simt(const __half *x, const __half
     }
 }
 
-// Launch with programmatic stream serialisation: the kernel's set-up overlaps its predecessor's tail (the kernel
-// calls pdl_wait() before touching memory). SH_PDL=0 launches the plain way.
-template <typename... KArgs, typename... Args>
-cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
-                       Args &&...args) {
-    static const bool pdl = [] {
-        const char *e = getenv("SH_PDL");
-        return !(e && atoi(e) == 0);
-    }();
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = grid;
-    cfg.blockDim = block;
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
-}
-
 template <int BN>
 bool set_smem_attr() {
     static bool done[sh::kMaxDevices] = {};
@@ -904,7 +882,7 @@ int launch_tc(const Plan &p, const CUtensorMap &mx, const CUtensorMap &mw, const
     if (!set_smem_attr<BN>()) return -1;
     const uint32_t units = p.tiles_m * p.tiles_n * p.splits;
     const uint32_t grid = min(units, (uint32_t)sh::state().num_sms);
-    return sh::cuda_ok(launch_pdl(k_gemm_tc<BN>, dim3(grid), dim3(kThreads), TileCfg<BN>::kSmem, st, mx, mw, mz, a),
+    return sh::cuda_ok(sh::launch_pdl(k_gemm_tc<BN>, dim3(grid), dim3(kThreads), TileCfg<BN>::kSmem, st, mx, mw, mz, a),
                        "sh_gemm launch")
                ? 0
                : -1;
@@ -925,7 +903,7 @@ int launch_pair(const Plan &p, const CUtensorMap &mx, const CUtensorMap &mw, con
     a.num_tiles = ((a.M + 255) / 256) * p.tiles_n;
     a.splits = 1;
     const uint32_t pairs = min(a.num_tiles, (uint32_t)sh::state().num_sms / 2);
-    return sh::cuda_ok(launch_pdl(k_gemm_tc2<BN>, dim3(2 * pairs), dim3(kPairThreads), PairCfg<BN>::kSmem, st, mx,
+    return sh::cuda_ok(sh::launch_pdl(k_gemm_tc2<BN>, dim3(2 * pairs), dim3(kPairThreads), PairCfg<BN>::kSmem, st, mx,
                                   mw, mz, a),
                        "sh_gemm launch (pair)")
                ? 0

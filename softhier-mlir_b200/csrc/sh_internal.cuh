@@ -12,6 +12,9 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 #include <stdio.h>
+#include <stdlib.h>
+
+#include <utility>
 
 #include "sh_ops.h"
 #include "sh_ops_cuda.h"
@@ -74,6 +77,29 @@ bool make_map_3d(CUtensorMap *m, const void *base, uint64_t batches, uint64_t ro
                  uint64_t batch_ld, uint32_t box_rows, uint32_t box_cols);
 
 inline bool aligned16(uint64_t p) { return (p & 15u) == 0; }
+
+// Launch with programmatic stream serialisation: the kernel's set-up overlaps its predecessor's tail (the kernel
+// calls pdl_wait() before touching memory). SH_PDL=0 launches the plain way.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                       Args &&...args) {
+    static const bool pdl = [] {
+        const char *e = getenv("SH_PDL");
+        return !(e && atoi(e) == 0);
+    }();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 
 }  // namespace sh
 

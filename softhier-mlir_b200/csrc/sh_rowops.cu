@@ -54,6 +54,8 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) k_layernorm_vec(__half *y
                                                                        const __half *b, const __half *g,
                                                                        const __half *be, uint32_t rows, uint32_t cols,
                                                                        uint32_t ld, float eps) {
+    pdl_launch_dependents();
+    pdl_wait();
     const uint32_t lane = threadIdx.x & 31;
     const uint32_t row = blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5);
     if (row >= rows) return;
@@ -108,6 +110,8 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) k_layernorm_any(__half *y
                                                                        const __half *b, const __half *g,
                                                                        const __half *be, uint32_t rows, uint32_t cols,
                                                                        uint32_t ld, float eps) {
+    pdl_launch_dependents();
+    pdl_wait();
     const uint32_t lane = threadIdx.x & 31;
     const uint32_t row = blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5);
     if (row >= rows) return;
@@ -140,6 +144,8 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) k_layernorm_any(__half *y
 template <int VPL>
 __global__ void __launch_bounds__(kWarpsPerBlock * 32) k_softmax_vec(__half *y, const __half *x, uint32_t rows,
                                                                      uint32_t cols, uint32_t ld, float scale) {
+    pdl_launch_dependents();
+    pdl_wait();
     const uint32_t lane = threadIdx.x & 31;
     const uint32_t row = blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5);
     if (row >= rows) return;
@@ -185,6 +191,8 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) k_softmax_vec(__half *y, 
 
 __global__ void __launch_bounds__(kWarpsPerBlock * 32) k_softmax_any(__half *y, const __half *x, uint32_t rows,
                                                                      uint32_t cols, uint32_t ld, float scale) {
+    pdl_launch_dependents();
+    pdl_wait();
     const uint32_t lane = threadIdx.x & 31;
     const uint32_t row = blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5);
     if (row >= rows) return;
@@ -229,6 +237,8 @@ template <int VPT, bool ADD>
 __global__ void __launch_bounds__(kRowThreads) k_layernorm_row(__half *y, __half *h, const __half *a, const __half *b,
                                                                const __half *g, const __half *be, uint32_t cols,
                                                                uint32_t ld, float eps) {
+    pdl_launch_dependents();
+    pdl_wait();
     __shared__ float red[kRowThreads / 32];
     const size_t row = blockIdx.x;
     const uint32_t cv = cols >> 3;
@@ -276,6 +286,8 @@ __global__ void __launch_bounds__(kRowThreads) k_layernorm_row(__half *y, __half
 template <int VPT, int NT = kRowThreads>
 __global__ void __launch_bounds__(NT) k_softmax_row(__half *y, const __half *x, uint32_t cols, uint32_t ld,
                                                     float scale) {
+    pdl_launch_dependents();
+    pdl_wait();
     __shared__ float red[kRowThreads / 32];
     const size_t row = blockIdx.x;
     const uint32_t cv = cols >> 3;
@@ -331,6 +343,8 @@ __device__ __forceinline__ float ew_apply(float x, float b, float s) {
 template <int OP>
 __global__ void k_ew_vec(__half *y, const __half *x, const __half *b, uint32_t rows, uint32_t cv, uint32_t ld,
                          float s) {
+    pdl_launch_dependents();
+    pdl_wait();
     const uint64_t total = (uint64_t)rows * cv;
     for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < total; i += (uint64_t)gridDim.x * blockDim.x) {
         const uint64_t r = i / cv, c = i - r * cv;
@@ -347,6 +361,8 @@ __global__ void k_ew_vec(__half *y, const __half *x, const __half *b, uint32_t r
 template <int OP>
 __global__ void k_ew_any(__half *y, const __half *x, const __half *b, uint32_t rows, uint32_t cols, uint32_t ld,
                          float s) {
+    pdl_launch_dependents();
+    pdl_wait();
     const uint64_t total = (uint64_t)rows * cols;
     for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < total; i += (uint64_t)gridDim.x * blockDim.x) {
         const uint64_t r = i / cols, c = i - r * cols;
@@ -451,10 +467,10 @@ void launch_ew(uint64_t y, uint64_t x, uint64_t b, uint32_t rows, uint32_t cols,
     if (OP == kBias) vec = vec && sh::aligned16(b);
     if (vec) {
         const uint32_t cv = cols / 8;
-        k_ew_vec<OP><<<ew_grid((uint64_t)rows * cv, 256), 256, 0, st>>>((__half *)y, (const __half *)x,
+        sh::launch_pdl(k_ew_vec<OP>, dim3(ew_grid((uint64_t)rows * cv, 256)), dim3(256), 0, st, (__half *)y, (const __half *)x,
                                                                         (const __half *)b, rows, cv, ld, s);
     } else {
-        k_ew_any<OP><<<ew_grid((uint64_t)rows * cols, 256), 256, 0, st>>>((__half *)y, (const __half *)x,
+        sh::launch_pdl(k_ew_any<OP>, dim3(ew_grid((uint64_t)rows * cols, 256)), dim3(256), 0, st, (__half *)y, (const __half *)x,
                                                                           (const __half *)b, rows, cols, ld, s);
     }
     sh::cuda_ok(cudaGetLastError(), name);
@@ -464,7 +480,7 @@ template <bool ADD, int VPL>
 void ln_vec_launch(uint64_t y, uint64_t h, uint64_t a, uint64_t b, uint64_t g, uint64_t be, uint32_t rows,
                    uint32_t cols, uint32_t ld, float eps, cudaStream_t st) {
     const uint32_t grid = (rows + kWarpsPerBlock - 1) / kWarpsPerBlock;
-    k_layernorm_vec<VPL, ADD><<<grid, kWarpsPerBlock * 32, 0, st>>>((__half *)y, (__half *)h, (const __half *)a,
+    sh::launch_pdl(k_layernorm_vec<VPL, ADD>, dim3(grid), dim3(kWarpsPerBlock * 32), 0, st, (__half *)y, (__half *)h, (const __half *)a,
                                                                      (const __half *)b, (const __half *)g,
                                                                      (const __half *)be, rows, cols, ld, eps);
 }
@@ -484,7 +500,7 @@ void launch_layernorm(uint64_t y, uint64_t h, uint64_t a, uint64_t b, uint64_t g
     if (vec && cols > 1024) {
         const uint32_t vpt = (cols / 8 + kRowThreads - 1) / kRowThreads;   // 2..4 vectors per thread
 #define SH_LNR(n) \
-    k_layernorm_row<n, ADD><<<rows, kRowThreads, 0, st>>>((__half *)y, (__half *)h, (const __half *)a, \
+    sh::launch_pdl(k_layernorm_row<n, ADD>, dim3(rows), dim3(kRowThreads), 0, st, (__half *)y, (__half *)h, (const __half *)a, \
                                                          (const __half *)b, (const __half *)g, (const __half *)be, cols, ld, eps)
         if (vpt <= 2) SH_LNR(2); else if (vpt <= 3) SH_LNR(3); else SH_LNR(4);
 #undef SH_LNR
@@ -501,7 +517,7 @@ void launch_layernorm(uint64_t y, uint64_t h, uint64_t a, uint64_t b, uint64_t g
         }
     } else {
         const uint32_t grid = (rows + kWarpsPerBlock - 1) / kWarpsPerBlock;
-        k_layernorm_any<ADD><<<grid, kWarpsPerBlock * 32, 0, st>>>((__half *)y, (__half *)h, (const __half *)a,
+        sh::launch_pdl(k_layernorm_any<ADD>, dim3(grid), dim3(kWarpsPerBlock * 32), 0, st, (__half *)y, (__half *)h, (const __half *)a,
                                                                    (const __half *)b, (const __half *)g,
                                                                    (const __half *)be, rows, cols, ld, eps);
     }
@@ -511,7 +527,7 @@ void launch_layernorm(uint64_t y, uint64_t h, uint64_t a, uint64_t b, uint64_t g
 template <int VPL>
 void sm_vec_launch(uint64_t y, uint64_t x, uint32_t rows, uint32_t cols, uint32_t ld, float scale, cudaStream_t st) {
     const uint32_t grid = (rows + kWarpsPerBlock - 1) / kWarpsPerBlock;
-    k_softmax_vec<VPL><<<grid, kWarpsPerBlock * 32, 0, st>>>((__half *)y, (const __half *)x, rows, cols, ld, scale);
+    sh::launch_pdl(k_softmax_vec<VPL>, dim3(grid), dim3(kWarpsPerBlock * 32), 0, st, (__half *)y, (const __half *)x, rows, cols, ld, scale);
 }
 
 }  // namespace
@@ -573,7 +589,7 @@ void sh_softmax_rows(uint64_t y, uint64_t x, uint32_t rows, uint32_t cols, uint3
     const bool vec = cols % 8 == 0 && cols <= 32u * 8u * kMaxVecPerLane && vec_ok(y, ld) && vec_ok(x, ld);
     if (vec && cols > 1024) {
         const uint32_t vpt = (cols / 8 + kRowThreads - 1) / kRowThreads;
-#define SH_SMR(n) k_softmax_row<n><<<rows, kRowThreads, 0, st>>>((__half *)y, (const __half *)x, cols, ld, scale)
+#define SH_SMR(n) sh::launch_pdl(k_softmax_row<n>, dim3(rows), dim3(kRowThreads), 0, st, (__half *)y, (const __half *)x, cols, ld, scale)
         if (vpt <= 2) SH_SMR(2); else if (vpt <= 3) SH_SMR(3); else SH_SMR(4);
 #undef SH_SMR
     } else if (vec) {
@@ -588,7 +604,7 @@ void sh_softmax_rows(uint64_t y, uint64_t x, uint32_t rows, uint32_t cols, uint3
         }
     } else {
         const uint32_t grid = (rows + kWarpsPerBlock - 1) / kWarpsPerBlock;
-        k_softmax_any<<<grid, kWarpsPerBlock * 32, 0, st>>>((__half *)y, (const __half *)x, rows, cols, ld, scale);
+        sh::launch_pdl(k_softmax_any, dim3(grid), dim3(kWarpsPerBlock * 32), 0, st, (__half *)y, (const __half *)x, rows, cols, ld, scale);
     }
     sh::cuda_ok(cudaGetLastError(), "sh_softmax_rows");
 }
