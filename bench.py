@@ -710,8 +710,60 @@ def run_rowops(args, local: int) -> dict:
     return {"metric": "row-op GB/s (HBM-resident)", "value": round(min(v["gbs"] for v in out.values()), 1),
             "unit": "GB/s (slowest op)", "n_gpus": 1, "higher_is_better": True, "dtype": "f16", "ops": out,
             "min_frac_hbm": worst, "peak": f"{src} copy {pk['hbm_gbs']} GB/s",
-            "config": {"workload": "BASELINE config 2 ops at 131072 x {768, 3072}",
+            "small": _rowops_small(torch, rt, stream),
+            "config": {"workload": "BASELINE config 2 ops at 131072 x {768, 3072}; 'small': the 256-row shapes",
                        "l2": "2 rotating buffer sets of 201 / 805 MB per operand (> 2 x L2)"}}
+
+
+# Simulated times of the reference's row ops at 256 x 768 on all 16 clusters, GVSoC at 1 GHz, ms
+# (docs/SIMULATOR_NOTES.md:184-192 of the reference)
+REF_GVSOC_ROWOPS_MS = {"layernorm": 0.149, "softmax": 0.145, "gelu": 0.123, "add": 0.022, "add_bias": 0.027,
+                       "scale": 0.017, "transpose": 0.025}
+
+
+def _rowops_small(torch, rt, stream, reps: int = 1000) -> dict:
+    """Config 2 at its own shapes (256 x 768 and 256 x 3072, L2-resident): microseconds per call, from 1000
+    back-to-back calls replayed from a CUDA graph, beside the reference's simulated time where it has one."""
+    from softhier_cuda import lib as L
+    lib, A, rows = rt.lib, L.SH_ALL, 256
+    res = {}
+    for cols in (768, 3072):
+        rt.reset()
+        x, b, y = rt.alloc(rows, cols), rt.alloc(rows, cols), rt.alloc(rows, cols)
+        g, be = rt.alloc(1, cols), rt.alloc(1, cols)
+        for i, (p, r, sd, mu) in enumerate(((x, rows, 1.0, 0.0), (b, rows, 1.0, 0.0), (g, 1, 0.02, 1.0),
+                                            (be, 1, 0.02, 0.0))):
+            lib.sh_cuda_fill_normal_fp16(p, r, cols, cols, 31 + i, mu, sd)
+        ops = {
+            "layernorm": lambda: lib.sh_layernorm(y, x, g, be, rows, cols, cols, 1e-6, A),
+            "softmax": lambda: lib.sh_softmax_rows(y, x, rows, cols, cols, 0.125, A),
+            "gelu": lambda: lib.sh_gelu(y, x, rows, cols, cols, A),
+            "add": lambda: lib.sh_add(y, x, b, rows, cols, cols, A),
+            "add_bias": lambda: lib.sh_add_bias(y, x, be, rows, cols, cols, A),
+            "scale": lambda: lib.sh_scale(y, x, rows, cols, cols, 0.125, A),
+            "transpose": lambda: lib.sh_transpose(y, x, rows, cols, cols, rows, A),
+        }
+        rt.activate(stream)
+        for name, fn in ops.items():
+            with torch.cuda.stream(stream):
+                for _ in range(3):
+                    fn()
+            g_ = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g_, stream=stream):
+                lib.sh_cuda_set_stream(torch.cuda.current_stream().cuda_stream)
+                for _ in range(reps):
+                    fn()
+            lib.sh_cuda_set_stream(stream.cuda_stream)
+            with torch.cuda.stream(stream):
+                g_.replay()
+                ms = _event_time(torch, stream, g_.replay, 3) / reps
+            del g_
+            ent = {"us": round(ms * 1e3, 3)}
+            if cols == 768 and name in REF_GVSOC_ROWOPS_MS:
+                ent["reference_gvsoc_us"] = REF_GVSOC_ROWOPS_MS[name] * 1e3
+            res[f"{name}_{rows}x{cols}"] = ent
+        rt.check()
+    return res
 
 
 def run_summa(args, rank: int, world: int, local: int) -> dict | None:
@@ -774,13 +826,34 @@ def run_summa(args, rank: int, world: int, local: int) -> dict | None:
         dist.destroy_process_group()
     if rank != 0:
         return None
-    return {"metric": "SUMMA 16384^3 TFLOP/s", "value": round(tf, 1), "unit": "TFLOP/s", "n_gpus": world,
+    extra = {}
+    if world == 1 and not args.no_cpu_baseline:
+        extra["cpu_baseline"] = summa_cpu_baseline(n)
+    return {**extra, "metric": "SUMMA 16384^3 TFLOP/s", "value": round(tf, 1), "unit": "TFLOP/s", "n_gpus": world,
             "steps": steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
             "scaling": "strong", "dtype": "f16", "frac_of_peak_per_gpu": round(tf / world / pk["bf16_tflops_sustained"], 3),
             "peak": f"{src} bf16 sustained {pk['bf16_tflops_sustained']} TFLOP/s per GPU",
             "peer_bytes_per_step_rank0": peer_bytes, "clocks": clock_info,
             "config": {"workload": "BASELINE config 4: distributed SUMMA", "n": n, "grid": f"{pr}x{pc}", "panel": kb,
                        "transport": "CUDA IPC + copy engines (cudaMemcpy2DAsync) over NVLink"}}
+
+
+def summa_cpu_baseline(n: int, sample: int = 4096) -> dict:
+    """Config 4 on the host: the reference's host check of a GEMM is an fp32 numpy matmul; one sample^3 product
+    with all BLAS threads, scaled to the n^3 FLOP of the full problem (TFLOP/s is size-independent enough at
+    4096^3 for a baseline)."""
+    import numpy as np
+    rng = np.random.default_rng(5)
+    a = rng.uniform(-1, 1, (sample, sample)).astype(np.float32)
+    b = rng.uniform(-1, 1, (sample, sample)).astype(np.float32)
+    a @ b
+    t0 = time.perf_counter()
+    a @ b
+    dt = time.perf_counter() - t0
+    tf = 2.0 * sample ** 3 / dt / 1e12
+    return {"value": round(tf, 4), "unit": "TFLOP/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"one fp32 {sample}^3 numpy matmul ({dt:.2f} s); the {n}^3 product at that rate would take "
+                      f"{2.0 * n ** 3 / tf / 1e12:.0f} s"}
 
 
 def main():
