@@ -33,6 +33,7 @@ constexpr int kPairThreads = 352;   // the 2-CTA kernel adds warp 10: forwards t
 constexpr uint32_t kEpiWarps = 8;
 
 constexpr uint32_t kEpiStageBytes = 8 * 4096;   // per epilogue warp: two 32 x 32 fp16 store tiles
+constexpr uint32_t kGroupM = 8;                  // default row-tiles per group of the tile order
 
 template <int BN>
 struct TileCfg {
@@ -50,6 +51,7 @@ struct GemmArgs {
     const __half *resid;
     uint32_t M, N, K, ldz, ldr, flags;
     uint32_t tiles_n, num_tiles, k_blocks, splits, kb_per_split;
+    uint32_t group_m;    // tile order: row-tiles per group (tile_coords)
     uint32_t vec;        // epilogue may use 16-byte accesses on z / bias / resid
     uint32_t tma_store;  // fp16 Z written by TMA stores of 32 x 32 tiles staged in shared memory
     float *ws;
@@ -64,6 +66,20 @@ struct GemmArgs {
     // SH_EPI_STATS_OUT: (sum, sum of squares) of each row's outputs per 64 columns, N / 64 pairs per row
     float2 *stats_out;
 };
+
+// Tile order of the persistent kernels: tiles are taken in groups of group_m row-tiles, and inside a group the
+// column-tiles advance slowest. The CTAs that run at the same time then share a few row-blocks of X and a few
+// column-blocks of W (each k-slice is fetched into L2 once per group), instead of sweeping every column-block of W
+// once per wave when W is wider than L2 holds.
+__device__ __forceinline__ void tile_coords(uint32_t tile, uint32_t tiles_m, uint32_t tiles_n, uint32_t group_m,
+                                            uint32_t &tm, uint32_t &tn) {
+    const uint32_t per_group = group_m * tiles_n;
+    const uint32_t g = tile / per_group, first = g * group_m;
+    const uint32_t gsz = min(group_m, tiles_m - first);
+    const uint32_t w = tile - g * per_group;
+    tm = first + w % gsz;
+    tn = w / gsz;
+}
 
 // mean and 1 / sqrt(var + eps) of a row of K values from its partial sums (SH_EPI_LN_IN)
 __device__ __forceinline__ float2 ln_row(const GemmArgs &a, uint32_t row) {
@@ -370,7 +386,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             bool ok = true;
             for (uint32_t u = blockIdx.x; ok && u < total_units; u += gridDim.x) {
                 const uint32_t tile = u / a.splits, split = u - tile * a.splits;
-                const uint32_t tm = tile / a.tiles_n, tn = tile - tm * a.tiles_n;
+                uint32_t tm, tn;
+                tile_coords(tile, a.num_tiles / a.tiles_n, a.tiles_n, a.group_m, tm, tn);
                 const uint32_t kb0 = split * a.kb_per_split;
                 const uint32_t kb1 = min(a.k_blocks, kb0 + a.kb_per_split);
                 for (uint32_t kb = kb0; kb < kb1; ++kb) {
@@ -454,7 +471,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t acc = 0, acc_phase = 0, es_phase = 0;
         for (uint32_t u = blockIdx.x; u < total_units; u += gridDim.x) {
             const uint32_t tile = u / a.splits, split = u - tile * a.splits;
-            const uint32_t tm = tile / a.tiles_n, tn = tile - tm * a.tiles_n;
+            uint32_t tm, tn;
+            tile_coords(tile, a.num_tiles / a.tiles_n, a.tiles_n, a.group_m, tm, tn);
             const uint32_t row = tm * BM + row_in_tile;
             const uint32_t row_base = tm * BM + quarter * 32;
             const uint32_t col0 = tn * BN + half * HB;
@@ -640,7 +658,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
             for (int s = 0; s < S; ++s) armed[s] = 2;
             bool ok = true;
             for (uint32_t u = pair; ok && u < total_units; u += npairs) {
-                const uint32_t tm = u / a.tiles_n, tn = u - tm * a.tiles_n;
+                uint32_t tm, tn;
+                tile_coords(u, a.num_tiles / a.tiles_n, a.tiles_n, a.group_m, tm, tn);
                 for (uint32_t kb = 0; kb < a.k_blocks; ++kb) {
                     if (!mbar_wait(&empty[stage], phase ^ 1u, abort, a.err)) {
                         ok = false;
@@ -727,7 +746,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
         if (a.tma_store && lane == 0) prefetch_tmap(&map_z);
         uint32_t acc = 0, acc_phase = 0;
         for (uint32_t u = pair; u < total_units; u += npairs) {
-            const uint32_t tm = u / a.tiles_n, tn = u - tm * a.tiles_n;
+            uint32_t tm, tn;
+            tile_coords(u, a.num_tiles / a.tiles_n, a.tiles_n, a.group_m, tm, tn);
             const uint32_t row = tm * 256 + row_in_tile;
             const uint32_t row_base = tm * 256 + rank * 128 + quarter * 32;
             const uint32_t col0 = tn * BN + half * HB;
@@ -910,6 +930,16 @@ int launch_pair(const Plan &p, const CUtensorMap &mx, const CUtensorMap &mw, con
                : -1;
 }
 
+// row-tiles per group of the tile order (SH_GEMM_GROUP_M overrides; 1 = plain row-major order)
+uint32_t gemm_group_m() {
+    static const uint32_t g = [] {
+        const char *e = getenv("SH_GEMM_GROUP_M");
+        const int v = e ? atoi(e) : (int)kGroupM;
+        return (uint32_t)(v < 1 ? 1 : v);
+    }();
+    return g;
+}
+
 uint32_t smem_of(int bn) {
     return bn == 256 ? TileCfg<256>::kSmem : bn == 128 ? TileCfg<128>::kSmem : bn == 64 ? TileCfg<64>::kSmem : 0;
 }
@@ -988,6 +1018,7 @@ int gemm_run(uint64_t x, uint64_t w, uint64_t z, uint32_t M, uint32_t N, uint32_
     }
     Plan p = make_plan(M, N, K, splits_req, s.num_sms, min_bn);
     a.tiles_n = p.tiles_n;
+    a.group_m = gemm_group_m();
     a.num_tiles = p.tiles_m * p.tiles_n;
     a.k_blocks = p.k_blocks;
     a.splits = p.splits;
@@ -1225,6 +1256,7 @@ extern "C" int sh_cuda_gemm_splitk_noalloc(uint64_t x, uint64_t w, uint64_t z, u
     }
     Plan p = make_plan(M, N, K, splits, num_sms);
     a.tiles_n = p.tiles_n;
+    a.group_m = gemm_group_m();
     a.num_tiles = p.tiles_m * p.tiles_n;
     a.k_blocks = p.k_blocks;
     a.splits = p.splits;
