@@ -101,7 +101,10 @@ def profile_traffic(kernel: str) -> float | None:
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 100 ms while the timed region runs."""
+    """nvidia-smi clocks / throttle reasons sampled every 20 ms while the timed region runs. start() returns once the
+    first sample has arrived (nvidia-smi takes a moment to start), so even a timed region of a few tens of
+    milliseconds gets samples; the samples taken before `mark()` (called where the timed region begins) are
+    dropped."""
 
     FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
@@ -112,16 +115,25 @@ class ClockSampler:
         self.index = vis.split(",")[local] if vis else str(local)
         self.proc = None
         self.lines: list[str] = []
+        self.first = 0
 
     def start(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                          "-i", self.index, "-lms", "100"], stdout=subprocess.PIPE,
+                                          "-i", self.index, "-lms", "20"], stdout=subprocess.PIPE,
                                          stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
         except OSError:
             self.proc = None
+            return
+        t0 = time.time()
+        while not self.lines and time.time() - t0 < 5.0 and self.proc.poll() is None:
+            time.sleep(0.01)
+
+    def mark(self):
+        """The timed region starts now."""
+        self.first = len(self.lines)
 
     def _read(self):
         for line in self.proc.stdout:
@@ -138,7 +150,7 @@ class ClockSampler:
         self.thread.join(timeout=2)
         sm, mx, reasons = [], None, set()
         names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        for ln in self.lines:
+        for ln in self.lines[self.first:]:
             parts = [p.strip() for p in ln.split(",")]
             if len(parts) < 7:
                 continue
@@ -271,10 +283,10 @@ def run_ours(args, rank: int, world: int, local: int) -> dict | None:
     # ---- timed region: inputs resident in HBM --------------------------------------------------------------------------
     clocks = ClockSampler(local)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks.start()
     barrier(world)
     torch.cuda.synchronize()
-    clocks.start()
-    time.sleep(0.05)
+    clocks.mark()
     e0.record(stream)
     for _ in range(args.steps):
         step()
@@ -768,7 +780,7 @@ def _rowops_small(torch, rt, stream, reps: int = 1000) -> dict:
 
 def run_summa(args, rank: int, world: int, local: int) -> dict | None:
     """Config 4: C = A B, M = N = K = 16384, A / B uniform [-1, 1) from the LCG, block-distributed over the default
-    grid of the world size (1x1, 1x2, 2x2, 2x4). Panels of min(K / pc, K / pr) columns are pulled from their owners
+    grid of the world size (1x1, 1x2, 2x2, 2x4). Two K-panels on a grid (one on one GPU) are pulled from their owners
     over NVLink by the copy engines while the tcgen05 GEMM accumulates the previous panel. value = 2 n^3 / (max over ranks of the step
     time)."""
     import torch
@@ -778,7 +790,7 @@ def run_summa(args, rank: int, world: int, local: int) -> dict | None:
     torch.cuda.set_device(local)
     n = args.summa_n
     pr, pc = SU.default_grid(world)
-    kb = min(n // pc, n // pr)    # the widest panel that never straddles two owners: fewest fp32 carry passes
+    kb = SU.default_panel(n, world)   # one panel on 1 GPU, two on a grid: one fp32 carry pass
     lay = SU.Layout(n, n, n, pr, pc, kb)
     rt = Runtime.open(local, arena_bytes=64 << 20)
     if world > 1:
@@ -800,10 +812,10 @@ def run_summa(args, rank: int, world: int, local: int) -> dict | None:
     rt.check()
     clocks = ClockSampler(local)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks.start()
     barrier(world)
     torch.cuda.synchronize()
-    clocks.start()
-    time.sleep(0.05)
+    clocks.mark()
     steps = args.steps
     e0.record(compute)
     for _ in range(steps):         # each step also pulls the next step's first panel (the last one's ends in e1)
@@ -819,8 +831,7 @@ def run_summa(args, rank: int, world: int, local: int) -> dict | None:
     flop = 2.0 * n ** 3
     pk, src = peaks()
     tf = flop / ms / 1e9
-    peer_bytes = sum((lay.Mb * kb * 2 if p.a_rank != rank else 0) + (kb * lay.Nb * 2 if p.b_rank != rank else 0)
-                     for p in su.sched)
+    peer_bytes = SU.panel_peer_bytes(lay, rank)
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()

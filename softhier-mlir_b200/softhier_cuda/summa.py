@@ -5,14 +5,19 @@ Rank (i, j) of a pr x pc grid (rank = i * pc + j) owns, of C = A B with A [M, K]
     A_ij = A[i Mb:(i+1) Mb, j Kc:(j+1) Kc]     Mb = M / pr, Kc = K / pc
     B_ij = B[i Kr:(i+1) Kr, j Nb:(j+1) Nb]     Kr = K / pr, Nb = N / pc
     C_ij = C[i Mb:(i+1) Mb, j Nb:(j+1) Nb]  =  sum over K-panels k of  A[i-rows, k] B[k, j-cols]
-The A panel of K-panel k lives on rank (i, k // Kc) (this rank's grid row), the B panel on rank (k // Kr, j) (its
-grid column). Instead of the reference's row / column multicasts, every rank PULLS the two panels it needs with the
-copy engines (CUDA IPC mappings of the owners' blocks + cudaMemcpy2DAsync on a copy stream: no SM is spent on the
-transfer), into double-buffered local panels, while the tcgen05 GEMM of the previous panel runs on the compute stream
-(C_ij += A_panel B_panel through the accumulate epilogue, carried in fp32 between panels and rounded to fp16 by the
-last one). Inputs are read-only during a step, so the step needs no
-cross-GPU synchronisation; ranks start at different panels (their own A panel first) to spread the pulls over the
-owners.
+The A columns of a K-panel [k0, k0 + kb) live on the ranks (i, *) of this rank's grid row (owner of column k:
+k // Kc), its B rows on the ranks (*, j) of its grid column (owner of row k: k // Kr); a panel may span several
+owners and is then made of pieces. Instead of the reference's row / column multicasts, every rank PULLS the pieces
+it needs with the copy engines (CUDA IPC mappings of the owners' blocks + cudaMemcpy2DAsync on a copy stream: no SM
+is spent on the transfer), into double-buffered local panels, while the tcgen05 GEMM of the previous panel runs on
+the compute stream (C_ij += A_panel B_panel through the accumulate epilogue, carried in fp32 between panels and
+rounded to fp16 by the last one). A panel that is one piece of this rank's own block is read in place. Inputs are
+read-only during a step, so the step needs no cross-GPU synchronisation; ranks start at the panel holding their own
+A block, to spread the pulls over the owners.
+
+Panel width: every extra panel costs an fp32 read + write of C_ij (the carry), so multi-GPU grids use two panels
+(`default_panel`): the second panel's pull overlaps the first panel's GEMM, and the first panel of the next step is
+pulled while the second GEMM runs.
 
 `panel_schedule` is the host-side logic shared by the GPU driver (`SummaGPU`) and the numpy reference driver used by
 the multi-process CPU tests (`summa_numpy`).
@@ -53,8 +58,8 @@ class Layout:
     def check(self) -> None:
         if self.M % self.pr or self.N % self.pc or self.K % self.pc or self.K % self.pr:
             raise ValueError(f"{self.M}x{self.N}x{self.K} does not split over a {self.pr}x{self.pc} grid")
-        if self.Kc % self.kb or self.Kr % self.kb:
-            raise ValueError(f"panel width {self.kb} must divide K/pc = {self.Kc} and K/pr = {self.Kr}")
+        if self.kb <= 0 or self.K % self.kb:
+            raise ValueError(f"panel width {self.kb} must divide K = {self.K}")
 
     def coords(self, rank: int) -> tuple[int, int]:
         return divmod(rank, self.pc)
@@ -64,12 +69,25 @@ class Layout:
 
 
 @dataclass(frozen=True)
+class Piece:
+    rank: int          # owner
+    src: int           # first column (A) / row (B) inside the owner's block
+    dst: int           # first column (A) / row (B) inside the panel
+    width: int         # columns (A) / rows (B)
+
+
+@dataclass(frozen=True)
 class Panel:
-    k0: int            # first K index of the panel
-    a_rank: int        # owner of A[i-rows, k0:k0+kb]
-    a_col: int         # its column offset inside the owner's A block
-    b_rank: int        # owner of B[k0:k0+kb, j-cols]
-    b_row: int         # its row offset inside the owner's B block
+    k0: int                    # first K index of the panel
+    a: tuple[Piece, ...]       # A[i-rows, k0:k0+kb] by owner, in K order
+    b: tuple[Piece, ...]       # B[k0:k0+kb, j-cols] by owner, in K order
+
+    def a_direct(self, rank: int) -> bool:
+        """The A panel is one piece of `rank`'s own block (read in place)."""
+        return len(self.a) == 1 and self.a[0].rank == rank
+
+    def b_direct(self, rank: int) -> bool:
+        return len(self.b) == 1 and self.b[0].rank == rank
 
 
 def default_grid(world: int) -> tuple[int, int]:
@@ -77,18 +95,39 @@ def default_grid(world: int) -> tuple[int, int]:
     return {1: (1, 1), 2: (1, 2), 4: (2, 2), 8: (2, 4)}.get(world, (1, world))
 
 
+def default_panel(K: int, world: int) -> int:
+    """One panel on one GPU; two on a grid (one fp32 carry pass, the second pull overlapped)."""
+    return K if world == 1 or K % 2 else K // 2
+
+
+def _pieces(k0: int, kb: int, block: int, owners: list[int]) -> tuple[Piece, ...]:
+    out = []
+    for idx, r in enumerate(owners):
+        lo, hi = max(k0, idx * block), min(k0 + kb, (idx + 1) * block)
+        if lo < hi:
+            out.append(Piece(r, lo - idx * block, lo - k0, hi - lo))
+    return tuple(out)
+
+
 def panel_schedule(lay: Layout, rank: int) -> list[Panel]:
-    """The K-panels rank (i, j) accumulates, in its order: starting with the first panel whose A block it owns."""
+    """The K-panels rank (i, j) accumulates, in its order: starting with the panel that holds its own A block."""
     lay.check()
     i, j = lay.coords(rank)
     n = lay.K // lay.kb
     start = (j * lay.Kc) // lay.kb
+    row_owners = [lay.rank_of(i, jj) for jj in range(lay.pc)]
+    col_owners = [lay.rank_of(ii, j) for ii in range(lay.pr)]
     out = []
     for t in range(n):
         k0 = ((start + t) % n) * lay.kb
-        ja, ib = k0 // lay.Kc, k0 // lay.Kr
-        out.append(Panel(k0, lay.rank_of(i, ja), k0 - ja * lay.Kc, lay.rank_of(ib, j), k0 - ib * lay.Kr))
+        out.append(Panel(k0, _pieces(k0, lay.kb, lay.Kc, row_owners), _pieces(k0, lay.kb, lay.Kr, col_owners)))
     return out
+
+
+def panel_peer_bytes(lay: Layout, rank: int) -> int:
+    """Bytes this rank pulls from other GPUs per step."""
+    return sum(sum(lay.Mb * q.width * 2 for q in p.a if q.rank != rank) +
+               sum(q.width * lay.Nb * 2 for q in p.b if q.rank != rank) for p in panel_schedule(lay, rank))
 
 
 def summa_numpy(lay: Layout, rank: int, a_blocks: dict, b_blocks: dict):
@@ -97,8 +136,12 @@ def summa_numpy(lay: Layout, rank: int, a_blocks: dict, b_blocks: dict):
     import numpy as np
     c = np.zeros((lay.Mb, lay.Nb), np.float32)
     for p in panel_schedule(lay, rank):
-        a = a_blocks[p.a_rank][:, p.a_col:p.a_col + lay.kb].astype(np.float32)
-        b = b_blocks[p.b_rank][p.b_row:p.b_row + lay.kb, :].astype(np.float32)
+        a = np.zeros((lay.Mb, lay.kb), np.float32)
+        b = np.zeros((lay.kb, lay.Nb), np.float32)
+        for q in p.a:
+            a[:, q.dst:q.dst + q.width] = a_blocks[q.rank][:, q.src:q.src + q.width]
+        for q in p.b:
+            b[q.dst:q.dst + q.width, :] = b_blocks[q.rank][q.src:q.src + q.width, :]
         c += a @ b
     return c
 
@@ -120,10 +163,11 @@ class SummaGPU:
         self.c = al(lay.Mb * lay.Nb * 2)
         # fp32 running sum of the panels (fp32 accumulation); C is rounded to fp16 once
         self.acc = al(lay.Mb * lay.Nb * 4) if lay.K // lay.kb > 1 else None
-        remote = any(p.a_rank != rank or p.b_rank != rank for p in self.sched)
-        self.a_pan = [al(lay.Mb * lay.kb * 2) for _ in range(2)] if remote else []
-        self.b_pan = [al(lay.kb * lay.Nb * 2) for _ in range(2)] if remote else []
-        if not (self.a_loc and self.b_loc and self.c) or (remote and not all(self.a_pan + self.b_pan)):
+        need_a_pan = any(not p.a_direct(rank) for p in self.sched)
+        need_b_pan = any(not p.b_direct(rank) for p in self.sched)
+        self.a_pan = [al(lay.Mb * lay.kb * 2) for _ in range(2)] if need_a_pan else []
+        self.b_pan = [al(lay.kb * lay.Nb * 2) for _ in range(2)] if need_b_pan else []
+        if not (self.a_loc and self.b_loc and self.c) or not all(self.a_pan + self.b_pan):
             raise RuntimeError("sh_cuda_ipc_alloc failed")
         ha, hb = ctypes.create_string_buffer(64), ctypes.create_string_buffer(64)
         if lib.sh_cuda_ipc_handle(self.a_loc, ha) or lib.sh_cuda_ipc_handle(self.b_loc, hb):
@@ -132,8 +176,8 @@ class SummaGPU:
         self.peer_a: dict[int, int] = {rank: self.a_loc}
         self.peer_b: dict[int, int] = {rank: self.b_loc}
         self.opened: list[int] = []
-        need_a = {p.a_rank for p in self.sched} - {rank}
-        need_b = {p.b_rank for p in self.sched} - {rank}
+        need_a = {q.rank for p in self.sched for q in p.a} - {rank}
+        need_b = {q.rank for p in self.sched for q in p.b} - {rank}
         for r, hA, hB in handles:
             for need, table, h in ((need_a, self.peer_a, hA), (need_b, self.peer_b, hB)):
                 if r in need:
@@ -171,23 +215,26 @@ class SummaGPU:
         def pull(idx: int):
             p, s = self.sched[idx], idx % 2
             pulled[s] = False
-            if p.a_rank == self.rank and p.b_rank == self.rank:
+            if p.a_direct(self.rank) and p.b_direct(self.rank):
                 return
             with torch.cuda.stream(self.copy):
                 if self._gemm_recorded[s]:
                     self.copy.wait_event(gemm_done[s])       # the last GEMM that read this slot is done
-                if p.a_rank != self.rank:
-                    lib.sh_cuda_copy2d(self.a_pan[s], lay.kb * 2, self.peer_a[p.a_rank] + 2 * p.a_col, lay.Kc * 2,
-                                       lay.kb * 2, lay.Mb, self.copy.cuda_stream)
-                if p.b_rank != self.rank:
-                    lib.sh_cuda_copy2d(self.b_pan[s], lay.Nb * 2, self.peer_b[p.b_rank] + 2 * p.b_row * lay.Nb,
-                                       lay.Nb * 2, lay.Nb * 2, lay.kb, self.copy.cuda_stream)
+                if not p.a_direct(self.rank):
+                    for q in p.a:                            # column pieces of the A panel (a local one too)
+                        lib.sh_cuda_copy2d(self.a_pan[s] + 2 * q.dst, lay.kb * 2, self.peer_a[q.rank] + 2 * q.src,
+                                           lay.Kc * 2, q.width * 2, lay.Mb, self.copy.cuda_stream)
+                if not p.b_direct(self.rank):
+                    for q in p.b:                            # row pieces of the B panel
+                        lib.sh_cuda_copy2d(self.b_pan[s] + 2 * q.dst * lay.Nb, lay.Nb * 2,
+                                           self.peer_b[q.rank] + 2 * q.src * lay.Nb, lay.Nb * 2, lay.Nb * 2,
+                                           q.width, self.copy.cuda_stream)
                 copy_done[s].record(self.copy)
             pulled[s] = True
 
         if self._prefetched:                      # panel 0 is already on its way (previous step's prefetch)
             p0 = self.sched[0]
-            pulled[0] = not (p0.a_rank == self.rank and p0.b_rank == self.rank)
+            pulled[0] = not (p0.a_direct(self.rank) and p0.b_direct(self.rank))
             self._prefetched = False
         else:
             pull(0)
@@ -203,12 +250,12 @@ class SummaGPU:
             with torch.cuda.stream(self.compute):
                 if pulled[s]:
                     self.compute.wait_event(copy_done[s])
-                if p.a_rank == self.rank:
-                    a, lda = self.a_loc + 2 * p.a_col, lay.Kc
+                if p.a_direct(self.rank):
+                    a, lda = self.a_loc + 2 * p.a[0].src, lay.Kc
                 else:
                     a, lda = self.a_pan[s], lay.kb
-                if p.b_rank == self.rank:
-                    b, ldb = self.b_loc + 2 * p.b_row * lay.Nb, lay.Nb
+                if p.b_direct(self.rank):
+                    b, ldb = self.b_loc + 2 * p.b[0].src * lay.Nb, lay.Nb
                 else:
                     b, ldb = self.b_pan[s], lay.Nb
                 last = idx == n - 1

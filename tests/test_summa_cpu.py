@@ -21,8 +21,10 @@ def _blocks(lay, A, B):
     return a, b
 
 
+# panel widths below, equal to and above the owners' block widths (K / pc, K / pr): panels of several pieces too
 @pytest.mark.parametrize("grid,kb", [((1, 1), 32), ((1, 2), 16), ((2, 2), 16), ((2, 4), 8), ((4, 2), 8),
-                                     ((2, 3), 8)])
+                                     ((2, 3), 8), ((2, 4), 48), ((2, 4), 24), ((1, 2), 96), ((4, 2), 32),
+                                     ((2, 3), 32)])
 def test_schedule_reproduces_matmul(grid, kb):
     pr, pc = grid
     M, N, K = 48 * pr, 40 * pc, 96
@@ -35,18 +37,35 @@ def test_schedule_reproduces_matmul(grid, kb):
         i, j = lay.coords(r)
         sched = SU.panel_schedule(lay, r)
         assert sorted(p.k0 for p in sched) == list(range(0, K, kb))          # every panel exactly once
-        assert sched[0].a_rank == r                                          # starts with its own A panel
-        assert all(lay.coords(p.a_rank)[0] == i and lay.coords(p.b_rank)[1] == j for p in sched)
+        assert any(q.rank == r for q in sched[0].a)                          # starts with its own A block
+        for p in sched:
+            for pieces, block, axis in ((p.a, lay.Kc, 0), (p.b, lay.Kr, 1)):
+                # pieces tile the panel in K order, each inside its owner's block, owners in this grid row / column
+                assert [q.dst for q in pieces] == list(np.cumsum([0] + [q.width for q in pieces[:-1]]))
+                assert sum(q.width for q in pieces) == kb
+                assert all(0 <= q.src and q.src + q.width <= block for q in pieces)
+                assert all(lay.coords(q.rank)[axis] == (i if axis == 0 else j) for q in pieces)
         C[i * lay.Mb:(i + 1) * lay.Mb, j * lay.Nb:(j + 1) * lay.Nb] = SU.summa_numpy(lay, r, a, b)
     np.testing.assert_allclose(C, A @ B, rtol=1e-4, atol=1e-4)
+
+
+def test_panel_peer_bytes_match_the_survey_figure():
+    # config 4 on 2x4 with two panels: (M/pr) K 2 (pc-1)/pc + K (N/pc) 2 (pr-1)/pr = 201 + 67 MB per GPU
+    n = 16384
+    lay = SU.Layout(n, n, n, 2, 4, SU.default_panel(n, 8))
+    assert lay.kb == n // 2
+    want = (n // 2) * n * 2 * 3 // 4 + n * (n // 4) * 2 // 2
+    assert all(SU.panel_peer_bytes(lay, r) == want for r in range(8))
+    assert SU.panel_peer_bytes(SU.Layout(n, n, n, 1, 1, n), 0) == 0
 
 
 def test_layout_rejects_bad_splits():
     with pytest.raises(ValueError):
         SU.Layout(100, 64, 64, 3, 1, 16).check()
     with pytest.raises(ValueError):
-        SU.Layout(64, 64, 96, 1, 2, 32).check()      # 32 does not divide K / pc = 48
+        SU.Layout(64, 64, 96, 1, 2, 36).check()      # 36 does not divide K = 96
     assert SU.default_grid(8) == (2, 4) and SU.default_grid(2) == (1, 2)
+    assert SU.default_panel(16384, 1) == 16384 and SU.default_panel(16384, 8) == 8192
 
 
 def _free_port() -> int:

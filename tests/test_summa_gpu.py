@@ -53,12 +53,15 @@ def test_summa_single_gpu_panels(gpu_lib, kb):
         su.close()
 
 
+# panel width 128: every panel one piece per operand; 512 = n / 2 (the default two panels): on 2x4 each A panel
+# spans two owners' blocks
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_summa_multi_gpu():
+@pytest.mark.parametrize("kb", [128, 512])
+def test_summa_multi_gpu(kb):
     world = 8 if torch.cuda.device_count() >= 8 else (4 if torch.cuda.device_count() >= 4 else 2)
-    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", SUMMA_KB=str(kb))
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
-           f"--nproc-per-node={world}", "--master-addr=127.0.0.1", "--master-port=29533",
+           f"--nproc-per-node={world}", "--master-addr=127.0.0.1", f"--master-port={29533 + kb % 7}",
            str(ROOT / "tests" / "summa_worker.py")]
     r = subprocess.run(cmd, capture_output=True, text=True, env=env, timeout=360)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
