@@ -591,13 +591,19 @@ __global__ void __launch_bounds__(kThreads, 1)
 // split-K (the caller picks this kernel only without it).
 constexpr int kPairStages = 6;
 
+// BN = 512: 256 x 512 pair tiles from two N = 256 MMAs per k-step into one accumulator (all 512 tensor-memory
+// columns): 25 % fewer operand bytes per MAC than 256 x 256, but the epilogue no longer overlaps the next tile's
+// main loop, so the planner uses it for long K loops only.
 template <int BN>
 struct PairCfg {
+    static constexpr int kStages = BN == 512 ? 4 : kPairStages;
+    static constexpr uint32_t kAcc = BN == 512 ? 1 : 2;          // accumulator buffers
+    static constexpr uint32_t kMmaN = BN < 256 ? BN : 256;       // N of one MMA; BN / kMmaN of them per k-step
     static constexpr uint32_t kABytes = 128 * BK * 2;          // this CTA's 128 rows
-    static constexpr uint32_t kBBytes = (BN / 2) * BK * 2;     // this CTA's BN/2 columns
+    static constexpr uint32_t kBBytes = (BN / 2) * BK * 2;     // this CTA's half of every MMA's columns
     static constexpr uint32_t kStageBytes = kABytes + kBBytes;
-    static constexpr uint32_t kTmemCols = 2 * BN;
-    static constexpr uint32_t kSmem = kPairStages * kStageBytes + kEpiStageBytes + 1024 + 256;
+    static constexpr uint32_t kTmemCols = kAcc * BN;
+    static constexpr uint32_t kSmem = kStages * kStageBytes + kEpiStageBytes + 1024 + 256;
 };
 
 template <int BN>
@@ -605,7 +611,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     k_gemm_tc2(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w,
                const __grid_constant__ CUtensorMap map_z, GemmArgs a) {
     using C = PairCfg<BN>;
-    constexpr int S = kPairStages;
+    constexpr int S = C::kStages;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
     uint8_t *smem = smem_raw + pad;
@@ -671,10 +677,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                     if (leader) mbar_arrive_expect_tx(&full[stage], 2 * C::kStageBytes);
                     armed[stage] = phase;
                     tma_load_2d_pair(sa, &map_x, bar, (int32_t)(kb * BK), (int32_t)(tm * 256 + rank * 128));
+                    // 64-column boxes: MMA h reads this CTA's kMmaN / 2 columns h kMmaN + rank kMmaN / 2 ..
+                    constexpr int kBoxesPerMma = C::kMmaN / 128;
 #pragma unroll
                     for (int c = 0; c < BN / 128; ++c)
                         tma_load_2d_pair(sb + c * (BK * 128), &map_w, bar,
-                                         (int32_t)(tn * BN + rank * (BN / 2) + c * 64), (int32_t)(kb * BK));
+                                         (int32_t)(tn * BN + (c / kBoxesPerMma) * C::kMmaN + rank * (C::kMmaN / 2) +
+                                                   (c % kBoxesPerMma) * 64),
+                                         (int32_t)(kb * BK));
                     if (++stage == S) {
                         stage = 0;
                         phase ^= 1u;
@@ -687,7 +697,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
         }
     } else if (warp == 1) {
         if (lane == 0 && leader) {
-            constexpr uint32_t idesc = umma_idesc_f16(256, BN, 0, 1);
+            constexpr uint32_t idesc = umma_idesc_f16(256, C::kMmaN, 0, 1);
             uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
             bool ok = true;
             for (uint32_t u = pair; ok && u < total_units; u += npairs) {
@@ -704,8 +714,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                     const uint32_t sb = sa + C::kABytes;
 #pragma unroll
                     for (int j = 0; j < BK / 16; ++j)
-                        umma_f16_ss_pair(d, sw128_desc(sa + j * 32, 16, 1024), sw128_desc(sb + j * 2048, BK * 128, 1024),
-                                         idesc, (kb > 0 || j > 0) ? 1u : 0u);
+#pragma unroll
+                        for (uint32_t h = 0; h < BN / C::kMmaN; ++h)
+                            umma_f16_ss_pair(d + h * C::kMmaN, sw128_desc(sa + j * 32, 16, 1024),
+                                             sw128_desc(sb + h * (C::kMmaN / 2) * BK * 2 + j * 2048, BK * 128, 1024),
+                                             idesc, (kb > 0 || j > 0) ? 1u : 0u);
                     umma_commit_pair_both(&empty[stage]);
                     if (++stage == S) {
                         stage = 0;
@@ -714,8 +727,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                 }
                 if (!ok) break;
                 umma_commit_pair_both(&tfull[acc]);
-                acc ^= 1u;
-                if (acc == 0) acc_phase ^= 1u;
+                if (++acc == C::kAcc) {
+                    acc = 0;
+                    acc_phase ^= 1u;
+                }
             }
             umma_commit_pair_both(mdone);   // both CTAs: every MMA the leader issued has completed
         }
@@ -731,8 +746,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
             for (uint32_t u = pair; u < total_units; u += npairs) {
                 if (!mbar_wait(&epi_done[acc], acc_phase, abort, a.err)) break;
                 mbar_arrive_cluster(tempty_leader[acc]);
-                acc ^= 1u;
-                if (acc == 0) acc_phase ^= 1u;
+                if (++acc == C::kAcc) {
+                    acc = 0;
+                    acc_phase ^= 1u;
+                }
             }
         }
     } else {
@@ -779,8 +796,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&epi_done[acc]);
-            acc ^= 1u;
-            if (acc == 0) acc_phase ^= 1u;
+            if (++acc == C::kAcc) {
+                acc = 0;
+                acc_phase ^= 1u;
+            }
         }
         if (lane == 0 && nst) bulk_wait_all();
     }
@@ -855,7 +874,8 @@ bool set_smem_attr() {
 }
 
 struct Plan {
-    bool pair = false;            // 2-CTA kernel, 256 x 256 tiles
+    bool pair = false;            // 2-CTA kernel, 256 x pair_bn tiles
+    int pair_bn = 256;
     int bn = 0;                   // 0: CUDA-core fallback
     uint32_t tiles_m = 0, tiles_n = 0, k_blocks = 0, splits = 1, kb_per_split = 0;
 };
@@ -893,6 +913,21 @@ Plan make_plan(uint32_t M, uint32_t N, uint32_t K, uint32_t splits_req, int num_
     if (p.splits == 1 && p.bn == 256 && pair_env != 0 &&
         (uint64_t)((M + 255) / 256) * p.tiles_n * 2 >= (uint64_t)num_sms)
         p.pair = true;
+    // 256 x 512 pair tiles for long K loops when N is a multiple of 512 and the tile waves cost no more: a wide
+    // tile takes ~1.5x a 256 x 256 one while the operand loads bound the main loop (SH_GEMM_PAIR_BN=256 / 512
+    // forces one width; 512 still needs N % 512 == 0)
+    static const int pair_bn_env = [] {
+        const char *e = getenv("SH_GEMM_PAIR_BN");
+        return e ? atoi(e) : 0;
+    }();
+    if (p.pair && N % 512 == 0 && pair_bn_env != 256) {
+        const uint64_t pairs = (uint64_t)num_sms / 2, rows = (M + 255) / 256;
+        const uint64_t w256 = (rows * p.tiles_n + pairs - 1) / pairs, w512 = (rows * (N / 512) + pairs - 1) / pairs;
+        if (pair_bn_env == 512 || (p.k_blocks >= 32 && 3 * w512 <= 2 * w256)) {
+            p.pair_bn = 512;
+            p.tiles_n = N / 512;
+        }
+    }
     return p;
 }
 
@@ -1047,7 +1082,7 @@ int gemm_run(uint64_t x, uint64_t w, uint64_t z, uint32_t M, uint32_t N, uint32_
         return -1;
     }
     if (!a.tma_store) mz = mx;   // not read by the kernel
-    if (p.pair) return launch_pair<256>(p, mx, mw, mz, a, st);
+    if (p.pair) return p.pair_bn == 512 ? launch_pair<512>(p, mx, mw, mz, a, st) : launch_pair<256>(p, mx, mw, mz, a, st);
     switch (p.bn) {
         case 256: return launch_tc<256>(p, mx, mw, mz, a, st);
         case 128: return launch_tc<128>(p, mx, mw, mz, a, st);

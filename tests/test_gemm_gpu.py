@@ -210,3 +210,30 @@ def test_pair_tiles(gpu_lib, M, N, K, flags):
     row-tiles) end with a partial group of the grouped tile order, 2816 x 4096 with 16 column-tiles per row."""
     got, want = _run(gpu_lib, M, N, K, flags=flags)
     _close(got, want, K)
+
+
+# Shapes the planner gives 256 x 512 pair tiles (N % 512 == 0, K >= 2048, and 1.5 x the wide waves <= the 256 x 256
+# waves on 74 SM pairs): 4096 x 4096 (4 vs 2 waves), 2816 x 2048 (11 row-tiles, ragged; 2 vs 1), 4096 x 2048 (2 vs 1).
+@pytest.mark.parametrize("M,N,K,flags", [(4096, 4096, 2048, 0), (2816, 2048, 4096, L.EPI_BIAS | L.EPI_RESIDUAL),
+                                         (4096, 2048, 2048, L.EPI_ACCUMULATE | L.EPI_BIAS)])
+def test_wide_pair_tiles(gpu_lib, M, N, K, flags):
+    got, want = _run(gpu_lib, M, N, K, flags=flags)
+    _close(got, want, K)
+
+
+def test_wide_pair_tiles_fp32_carry(gpu_lib):
+    """The SUMMA panel pattern on 256 x 512 tiles: fp32 out, then fp32 carry-in rounded to fp16 once."""
+    rt, lib = gpu_lib, gpu_lib.lib
+    rt.reset()
+    M, N, Kp = 4096, 2048, 2048
+    xs = [lcg.uniform_fp16(M, Kp, 70 + i) for i in range(2)]
+    ws = [lcg.uniform_fp16(Kp, N, 80 + i) for i in range(2)]
+    dx = [rt.upload(x) for x in xs]
+    dw = [rt.upload(w) for w in ws]
+    acc = rt.alloc_bytes(M * N * 4)
+    z = rt.alloc(M, N)
+    assert lib.sh_cuda_gemm(dx[0], dw[0], acc, M, N, Kp, Kp, N, N, 0, 0, 0, L.EPI_F32_OUT, 1) == 0
+    assert lib.sh_cuda_gemm(dx[1], dw[1], z, M, N, Kp, Kp, N, N, 0, acc, N, L.EPI_ACC_F32_IN, 1) == 0
+    rt.check()
+    want = sum(ops.gemm(x, w) for x, w in zip(xs, ws))
+    _close(rt.get(z, M, N), want, 2 * Kp)
