@@ -780,9 +780,9 @@ def _rowops_small(torch, rt, stream, reps: int = 1000) -> dict:
 
 def run_summa(args, rank: int, world: int, local: int) -> dict | None:
     """Config 4: C = A B, M = N = K = 16384, A / B uniform [-1, 1) from the LCG, block-distributed over the default
-    grid of the world size (1x1, 1x2, 2x2, 2x4). Two K-panels on a grid (one on one GPU) are pulled from their owners
-    over NVLink by the copy engines while the tcgen05 GEMM accumulates the previous panel. value = 2 n^3 / (max over ranks of the step
-    time)."""
+    grid of the world size (1x1, 1x2, 2x2, 2x4). One K-panel per step is pulled from its owners over NVLink by the
+    copy engines while the tcgen05 GEMM of the previous step runs; every timed step does one full set of pulls and
+    one GEMM. value = 2 n^3 / (max over ranks of the step time)."""
     import torch
     from softhier_cuda import summa as SU
     from softhier_cuda.runtime import Runtime
@@ -790,7 +790,7 @@ def run_summa(args, rank: int, world: int, local: int) -> dict | None:
     torch.cuda.set_device(local)
     n = args.summa_n
     pr, pc = SU.default_grid(world)
-    kb = SU.default_panel(n, world)   # one panel on 1 GPU, two on a grid: one fp32 carry pass
+    kb = SU.default_panel(n, world)   # one panel per step: no fp32 carry; pulled during the previous step
     lay = SU.Layout(n, n, n, pr, pc, kb)
     rt = Runtime.open(local, arena_bytes=64 << 20)
     if world > 1:

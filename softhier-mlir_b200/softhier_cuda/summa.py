@@ -15,9 +15,9 @@ rounded to fp16 by the last one). A panel that is one piece of this rank's own b
 read-only during a step, so the step needs no cross-GPU synchronisation; ranks start at the panel holding their own
 A block, to spread the pulls over the owners.
 
-Panel width: every extra panel costs an fp32 read + write of C_ij (the carry), so multi-GPU grids use two panels
-(`default_panel`): the second panel's pull overlaps the first panel's GEMM, and the first panel of the next step is
-pulled while the second GEMM runs.
+Panel width: every extra panel costs an fp32 read + write of C_ij (the carry), so the default is one panel per step
+(`default_panel`). Panel slots alternate by a running count across steps, so the next step's panel is pulled while
+this step's GEMM runs. Every step still does one full set of pulls and one GEMM.
 
 `panel_schedule` is the host-side logic shared by the GPU driver (`SummaGPU`) and the numpy reference driver used by
 the multi-process CPU tests (`summa_numpy`).
@@ -96,8 +96,10 @@ def default_grid(world: int) -> tuple[int, int]:
 
 
 def default_panel(K: int, world: int) -> int:
-    """One panel on one GPU; two on a grid (one fp32 carry pass, the second pull overlapped)."""
-    return K if world == 1 or K % 2 else K // 2
+    """One panel per step on any grid: no fp32 carry pass, and the pull of a step's whole panel overlaps the previous
+    step's GEMM (SummaGPU.step with prefetch_next). Two or more panels also overlap pulls inside a step, at the
+    cost of an fp32 read + write of C_ij per extra panel."""
+    return K
 
 
 def _pieces(k0: int, kb: int, block: int, owners: list[int]) -> tuple[Piece, ...]:
@@ -198,9 +200,10 @@ class SummaGPU:
         self.barrier()        # every block exists before any rank pulls from it
 
     def step(self, torch, prefetch_next: bool = False) -> int:
-        """C_ij = sum over panels (enqueued; returns 0 or the first failing return code). With prefetch_next the
-        first panel of the next step (the same panels: inputs are read-only) is pulled while this step's last GEMM
-        runs, so that a run of steps keeps the copy engines busy across step boundaries."""
+        """C_ij = sum over panels (enqueued; returns 0 or the first failing return code). Panels alternate between
+        two buffer slots by a running count, across steps too. With prefetch_next the first panel of the next step
+        (the same panels: inputs are read-only) is pulled while this step's last GEMM runs, so that a run of steps
+        keeps the copy engines busy across step boundaries; with one panel per step that is the whole next pull."""
         lay, lib = self.lay, self.lib
         lib.sh_cuda_set_stream(self.compute.cuda_stream)
         if not hasattr(self, "_ev"):
@@ -208,12 +211,13 @@ class SummaGPU:
                         "gemm": [torch.cuda.Event(), torch.cuda.Event()]}
             self._gemm_recorded = [False, False]
             self._prefetched = False
+            self._count = 0          # panels enqueued so far: panel t of the run uses slot t % 2
         copy_done, gemm_done = self._ev["copy"], self._ev["gemm"]
         pulled = [False, False]
-        n = len(self.sched)
+        n, base = len(self.sched), self._count
 
-        def pull(idx: int):
-            p, s = self.sched[idx], idx % 2
+        def pull(idx: int, s: int):
+            p = self.sched[idx]
             pulled[s] = False
             if p.a_direct(self.rank) and p.b_direct(self.rank):
                 return
@@ -234,18 +238,19 @@ class SummaGPU:
 
         if self._prefetched:                      # panel 0 is already on its way (previous step's prefetch)
             p0 = self.sched[0]
-            pulled[0] = not (p0.a_direct(self.rank) and p0.b_direct(self.rank))
+            pulled[base % 2] = not (p0.a_direct(self.rank) and p0.b_direct(self.rank))
             self._prefetched = False
         else:
-            pull(0)
+            pull(0, base % 2)
         rc = 0
         for idx, p in enumerate(self.sched):
-            s = idx % 2
+            s = (base + idx) % 2
             if idx + 1 < n:
-                pull(idx + 1)
-            elif prefetch_next and n % 2 == 0 and n > 1:
-                # the next step's panel 0 goes to slot 0, last read by this step's panel n - 2
-                pull(0)
+                pull(idx + 1, (base + idx + 1) % 2)
+            elif prefetch_next:
+                # the next step's panel 0 goes to the other slot, last read by this step's panel n - 2 (or by the
+                # previous step's last panel when n == 1)
+                pull(0, (base + n) % 2)
                 self._prefetched = True
             with torch.cuda.stream(self.compute):
                 if pulled[s]:
@@ -270,6 +275,7 @@ class SummaGPU:
                 rc = rc or lib.sh_cuda_gemm(a, b, z, lay.Mb, lay.Nb, lay.kb, lda, ldb, lay.Nb, 0, res, lay.Nb, flags, 1)
                 gemm_done[s].record(self.compute)
                 self._gemm_recorded[s] = True
+        self._count += n
         return rc
 
     def finish(self, torch) -> None:

@@ -49,11 +49,11 @@ def test_schedule_reproduces_matmul(grid, kb):
     np.testing.assert_allclose(C, A @ B, rtol=1e-4, atol=1e-4)
 
 
-def test_panel_peer_bytes_match_the_survey_figure():
-    # config 4 on 2x4 with two panels: (M/pr) K 2 (pc-1)/pc + K (N/pc) 2 (pr-1)/pr = 201 + 67 MB per GPU
+@pytest.mark.parametrize("kb", [16384, 8192, 4096])
+def test_panel_peer_bytes_match_the_survey_figure(kb):
+    # config 4 on 2x4, any panel width: (M/pr) K 2 (pc-1)/pc + K (N/pc) 2 (pr-1)/pr = 201 + 67 MB per GPU
     n = 16384
-    lay = SU.Layout(n, n, n, 2, 4, SU.default_panel(n, 8))
-    assert lay.kb == n // 2
+    lay = SU.Layout(n, n, n, 2, 4, kb)
     want = (n // 2) * n * 2 * 3 // 4 + n * (n // 4) * 2 // 2
     assert all(SU.panel_peer_bytes(lay, r) == want for r in range(8))
     assert SU.panel_peer_bytes(SU.Layout(n, n, n, 1, 1, n), 0) == 0
@@ -65,7 +65,7 @@ def test_layout_rejects_bad_splits():
     with pytest.raises(ValueError):
         SU.Layout(64, 64, 96, 1, 2, 36).check()      # 36 does not divide K = 96
     assert SU.default_grid(8) == (2, 4) and SU.default_grid(2) == (1, 2)
-    assert SU.default_panel(16384, 1) == 16384 and SU.default_panel(16384, 8) == 8192
+    assert SU.default_panel(16384, 1) == 16384 and SU.default_panel(16384, 8) == 16384
 
 
 def _free_port() -> int:

@@ -53,10 +53,10 @@ def test_summa_single_gpu_panels(gpu_lib, kb):
         su.close()
 
 
-# panel width 128: every panel one piece per operand; 512 = n / 2 (the default two panels): on 2x4 each A panel
-# spans two owners' blocks
+# panel width 128: every panel one piece per operand; 512 = n / 2: on 2x4 each A panel spans two owners' blocks;
+# 1024 = n (the default): one panel per step, pulled during the previous step's GEMM
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("kb", [128, 512])
+@pytest.mark.parametrize("kb", [128, 512, 1024])
 def test_summa_multi_gpu(kb):
     world = 8 if torch.cuda.device_count() >= 8 else (4 if torch.cuda.device_count() >= 4 else 2)
     env = dict(os.environ, NCCL_NVLS_ENABLE="0", SUMMA_KB=str(kb))
