@@ -101,23 +101,65 @@ def profile_traffic(kernel: str) -> float | None:
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 20 ms while the timed region runs. start() returns once the
-    first sample has arrived (nvidia-smi takes a moment to start), so even a timed region of a few tens of
-    milliseconds gets samples; the samples taken before `mark()` (called where the timed region begins) are
-    dropped."""
+    """SM clock, power and clock-event reasons of this rank's GPU, sampled while the timed region runs.
+
+    NVML (read-only queries) polled every 2 ms from a thread, so even a timed region of a few milliseconds gets
+    samples; the GPU is matched by UUID. Without NVML: nvidia-smi every 20 ms. start() returns once the first sample
+    exists; mark() is called where the timed region begins and earlier samples are dropped."""
 
     FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
               "clocks_event_reasons.sw_power_cap")
+    REASONS = (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40), ("sw_thermal_slowdown", 0x20),
+               ("sw_power_cap", 0x4))
 
     def __init__(self, local: int):
         vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+        self.local = local
         self.index = vis.split(",")[local] if vis else str(local)
         self.proc = None
+        self.nvml = None
+        self.samples: list[tuple[float, float, int]] = []    # (sm MHz, max MHz, reason bits)
         self.lines: list[str] = []
         self.first = 0
+        self.stop_flag = threading.Event()
+
+    def _nvml_handle(self):
+        import pynvml
+        import torch
+        pynvml.nvmlInit()
+        uuid = str(torch.cuda.get_device_properties(self.local).uuid)
+        for key in (uuid, "GPU-" + uuid):
+            try:
+                return pynvml, pynvml.nvmlDeviceGetHandleByUUID(key)
+            except pynvml.NVMLError:
+                continue
+        return pynvml, pynvml.nvmlDeviceGetHandleByIndex(int(self.index))
 
     def start(self):
+        try:
+            nv, h = self._nvml_handle()
+            reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons",
+                              getattr(nv, "nvmlDeviceGetCurrentClocksThrottleReasons", None))
+            mx = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+
+            def poll():
+                while not self.stop_flag.is_set():
+                    try:
+                        self.samples.append((float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)), mx,
+                                             int(reasons(h)) if reasons else 0))
+                    except nv.NVMLError:
+                        pass
+                    time.sleep(0.002)
+            self.nvml = nv
+            self.thread = threading.Thread(target=poll, daemon=True)
+            self.thread.start()
+            t0 = time.time()
+            while not self.samples and time.time() - t0 < 2.0:
+                time.sleep(0.001)
+            return
+        except Exception:   # no NVML here: nvidia-smi below
+            self.nvml = None
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                                           "-i", self.index, "-lms", "20"], stdout=subprocess.PIPE,
@@ -133,13 +175,25 @@ class ClockSampler:
 
     def mark(self):
         """The timed region starts now."""
-        self.first = len(self.lines)
+        self.first = len(self.samples) if self.nvml else len(self.lines)
 
     def _read(self):
         for line in self.proc.stdout:
             self.lines.append(line.strip())
 
     def stop(self) -> dict:
+        if self.nvml:
+            self.stop_flag.set()
+            self.thread.join(timeout=2)
+            got = self.samples[self.first:]
+            try:
+                self.nvml.nvmlShutdown()
+            except Exception:
+                pass
+            reasons = sorted({nm for _, _, bits in got for nm, b in self.REASONS if bits & b})
+            return {"sm_mhz": statistics.median(c for c, _, _ in got) if got else None,
+                    "sm_max_mhz": got[0][1] if got else None, "samples": len(got), "reasons": reasons,
+                    "source": "nvml, 2 ms"}
         if not self.proc:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.proc.terminate()
@@ -163,7 +217,7 @@ class ClockSampler:
                 if val.lower().startswith("active"):
                     reasons.add(nm)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "samples": len(sm),
-                "reasons": sorted(reasons)}
+                "reasons": sorted(reasons), "source": "nvidia-smi, 20 ms"}
 
 
 # ---- the GPU arm -----------------------------------------------------------------------------------------------------
