@@ -1,8 +1,8 @@
-"""Runs a small encoder forward (2 SigLIP-base layers, B = 12: 2-CTA and 1-CTA GEMMs, tcgen05 attention, LayerNorm)
-and one wide GEMM (2816 x 4096 x 256: 11 x 16 pair tiles, a partial tile group) on GPU 0 and prints the SHA-1 of
-their output bytes. tests/test_launch_modes_gpu.py runs it under different launch settings (SH_PDL,
-SH_GEMM_GROUP_M), which are read once per process, and requires identical bytes: the launch mode and the tile order
-must not change any result."""
+"""Runs a small encoder forward (2 SigLIP-base layers, B = 12: 2-CTA and 1-CTA GEMMs, tcgen05 attention, LayerNorm),
+one wide GEMM (2816 x 4096 x 256: 11 x 16 pair tiles, a partial tile group) and one long-K GEMM (4096 x 4096 x
+2048: 256 x 512 pair tiles) on GPU 0 and prints the SHA-1 of their output bytes. tests/test_launch_modes_gpu.py runs it under different launch settings (SH_PDL,
+SH_GEMM_GROUP_M, SH_GEMM_PAIR_BN), which are read once per process, and requires identical bytes: the launch mode,
+the tile order and the tile width must not change any result."""
 from __future__ import annotations
 
 import hashlib
@@ -45,8 +45,17 @@ def main():
     err = float(np.abs(gem.astype(np.float32) - want).max())
     if err > 2e-2 + 2.0 ** -10 * float(np.abs(want).max()):
         raise AssertionError(f"wide GEMM max err {err}")
+    # 4096 x 4096 x 2048: the planner's 256 x 512 pair tiles (SH_GEMM_PAIR_BN=256 forces 256 x 256)
+    M2, N2, K2 = 4096, 4096, 2048
+    a2, w2, z2 = rt.alloc(M2, K2), rt.alloc(K2, N2), rt.alloc(M2, N2)
+    lib.sh_test_fill_fp16(a2, M2, K2, K2, 5, -1024, 1023, 1.0 / 1024)
+    lib.sh_test_fill_fp16(w2, K2, N2, N2, 6, -1024, 1023, 1.0 / 1024)
+    if lib.sh_cuda_gemm(a2, w2, z2, M2, N2, K2, K2, N2, N2, 0, 0, N2, 0, 0):
+        raise RuntimeError(lib.sh_cuda_last_error_string().decode())
+    rt.check()
+    wide = rt.get(z2, M2, N2)
     h = lambda t: hashlib.sha1(np.ascontiguousarray(t).view(np.uint8).tobytes()).hexdigest()  # noqa: E731
-    print(f"HASH {h(enc)} {h(gem)}", flush=True)
+    print(f"HASH {h(enc)} {h(gem)} {h(wide)}", flush=True)
 
 
 if __name__ == "__main__":
