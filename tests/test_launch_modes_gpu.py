@@ -1,7 +1,7 @@
 """Launch settings change timing only: programmatic dependent launch on / off (SH_PDL), the GEMM tile order
 (SH_GEMM_GROUP_M: 1 = row-major, default 8 = grouped) and the pair tile width (SH_GEMM_PAIR_BN: 256 instead of the
-planner's 512 for long K) give bit-identical encoder and GEMM outputs. Each setting is
-read once per process, so every variant runs in its own process (tests/launch_modes_worker.py)."""
+planner's 512 for long K) give bit-identical encoder and GEMM outputs. Each setting is read once per process, so
+every variant runs in its own process (tests/launch_modes_worker.py)."""
 from __future__ import annotations
 
 import os
