@@ -52,6 +52,7 @@ struct GemmArgs {
     uint32_t M, N, K, ldz, ldr, flags;
     uint32_t tiles_n, num_tiles, k_blocks, splits, kb_per_split;
     uint32_t group_m;    // tile order: row-tiles per group (tile_coords)
+    uint32_t full_units, num_units;   // 2-CTA kernel: whole tiles below full_units, N-halves of the rest (pair_unit)
     uint32_t vec;        // epilogue may use 16-byte accesses on z / bias / resid
     uint32_t tma_store;  // fp16 Z written by TMA stores of 32 x 32 tiles staged in shared memory
     float *ws;
@@ -606,6 +607,24 @@ struct PairCfg {
     static constexpr uint32_t kSmem = kStages * kStageBytes + kEpiStageBytes + 1024 + 256;
 };
 
+// Work unit u of the 2-CTA kernel: whole tile u below a.full_units; past it, one kMmaN-wide column slice (h0) of
+// the remaining tiles, BN / kMmaN units per tile, so that a short last wave of wide tiles runs as a fuller wave of
+// narrower units. Every output element still accumulates the same MMAs in the same order.
+template <int BN>
+__device__ __forceinline__ void pair_unit(const GemmArgs &a, uint32_t u, uint32_t &tile, uint32_t &h0, uint32_t &nh) {
+    constexpr uint32_t NH = BN / PairCfg<BN>::kMmaN;
+    if (u < a.full_units) {
+        tile = u;
+        h0 = 0;
+        nh = NH;
+    } else {
+        const uint32_t t = u - a.full_units;
+        tile = a.full_units + t / NH;
+        h0 = t % NH;
+        nh = 1;
+    }
+}
+
 template <int BN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     k_gemm_tc2(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w,
@@ -651,7 +670,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     cluster_sync_all();     // both CTAs' barriers exist before any peer signal reaches them
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
-    const uint32_t total_units = a.num_tiles;
+    const uint32_t total_units = a.num_units;
     pdl_launch_dependents();
     pdl_wait();
 
@@ -664,8 +683,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
             for (int s = 0; s < S; ++s) armed[s] = 2;
             bool ok = true;
             for (uint32_t u = pair; ok && u < total_units; u += npairs) {
-                uint32_t tm, tn;
-                tile_coords(u, a.num_tiles / a.tiles_n, a.tiles_n, a.group_m, tm, tn);
+                uint32_t tile, h0, nh, tm, tn;
+                pair_unit<BN>(a, u, tile, h0, nh);
+                tile_coords(tile, a.num_tiles / a.tiles_n, a.tiles_n, a.group_m, tm, tn);
+                const uint32_t stage_tx = 2 * (C::kABytes + nh * (C::kMmaN / 2) * BK * 2);   // both CTAs' bytes
                 for (uint32_t kb = 0; kb < a.k_blocks; ++kb) {
                     if (!mbar_wait(&empty[stage], phase ^ 1u, abort, a.err)) {
                         ok = false;
@@ -674,17 +695,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                     uint8_t *sa = smem + stage * C::kStageBytes;
                     uint8_t *sb = sa + C::kABytes;
                     const uint32_t bar = mapa_shared(smem_u32(&full[stage]), 0);
-                    if (leader) mbar_arrive_expect_tx(&full[stage], 2 * C::kStageBytes);
+                    if (leader) mbar_arrive_expect_tx(&full[stage], stage_tx);
                     armed[stage] = phase;
                     tma_load_2d_pair(sa, &map_x, bar, (int32_t)(kb * BK), (int32_t)(tm * 256 + rank * 128));
                     // 64-column boxes: MMA h reads this CTA's kMmaN / 2 columns h kMmaN + rank kMmaN / 2 ..
                     constexpr int kBoxesPerMma = C::kMmaN / 128;
 #pragma unroll
-                    for (int c = 0; c < BN / 128; ++c)
+                    for (int c = 0; c < BN / 128; ++c) {
+                        const uint32_t h = c / kBoxesPerMma;
+                        if (h < h0 || h >= h0 + nh) continue;   // a column slice loads its own MMA's boxes only
                         tma_load_2d_pair(sb + c * (BK * 128), &map_w, bar,
-                                         (int32_t)(tn * BN + (c / kBoxesPerMma) * C::kMmaN + rank * (C::kMmaN / 2) +
+                                         (int32_t)(tn * BN + h * C::kMmaN + rank * (C::kMmaN / 2) +
                                                    (c % kBoxesPerMma) * 64),
                                          (int32_t)(kb * BK));
+                    }
                     if (++stage == S) {
                         stage = 0;
                         phase ^= 1u;
@@ -701,6 +725,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
             uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
             bool ok = true;
             for (uint32_t u = pair; ok && u < total_units; u += npairs) {
+                uint32_t tile, h0, nh;
+                pair_unit<BN>(a, u, tile, h0, nh);
                 if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort, a.err)) break;
                 tc_fence_after();
                 const uint32_t d = tmem_base + acc * BN;
@@ -716,6 +742,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                     for (int j = 0; j < BK / 16; ++j)
 #pragma unroll
                         for (uint32_t h = 0; h < BN / C::kMmaN; ++h)
+                            if (h >= h0 && h < h0 + nh)
                             umma_f16_ss_pair(d + h * C::kMmaN, sw128_desc(sa + j * 32, 16, 1024),
                                              sw128_desc(sb + h * (C::kMmaN / 2) * BK * 2 + j * 2048, BK * 128, 1024),
                                              idesc, (kb > 0 || j > 0) ? 1u : 0u);
@@ -755,7 +782,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     } else {
         const uint32_t quarter = warp & 3u;
         const uint32_t half = (warp - 2u) >> 2;
-        constexpr uint32_t HB = BN / 2;
         const uint32_t row_in_tile = rank * 128 + quarter * 32 + lane;
         const bool want_res = (a.flags & SH_EPI_RESIDUAL) != 0;
         uint8_t *stg = epi_stage + (warp - 2u) * 4096u;
@@ -763,11 +789,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
         if (a.tma_store && lane == 0) prefetch_tmap(&map_z);
         uint32_t acc = 0, acc_phase = 0;
         for (uint32_t u = pair; u < total_units; u += npairs) {
-            uint32_t tm, tn;
-            tile_coords(u, a.num_tiles / a.tiles_n, a.tiles_n, a.group_m, tm, tn);
+            uint32_t tile, h0, nh, tm, tn;
+            pair_unit<BN>(a, u, tile, h0, nh);
+            tile_coords(tile, a.num_tiles / a.tiles_n, a.tiles_n, a.group_m, tm, tn);
+            const uint32_t HB = nh * (C::kMmaN / 2);   // columns per warp: this unit's columns, split in two halves
             const uint32_t row = tm * 256 + row_in_tile;
             const uint32_t row_base = tm * 256 + rank * 128 + quarter * 32;
-            const uint32_t col0 = tn * BN + half * HB;
+            const uint32_t col0 = tn * BN + h0 * C::kMmaN + half * HB;
             uint4 res[4] = {};
             const bool res_vec = want_res && a.vec && row < a.M;
             if (res_vec && col0 + 32 <= a.N) load32(a.resid + (size_t)row * a.ldr + col0, res);
@@ -775,7 +803,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
             float2 st = make_float2(0.f, 0.f);
             if (!mbar_wait(&tfull[acc], acc_phase, abort, a.err)) break;
             tc_fence_after();
-            const uint32_t taddr = tmem_base + ((quarter * 32u) << 16) + acc * BN + half * HB;
+            const uint32_t taddr = tmem_base + ((quarter * 32u) << 16) + acc * BN + h0 * C::kMmaN + half * HB;
 #pragma unroll 1
             for (uint32_t c = 0; c < HB / 32; ++c) {
                 uint32_t r[32];
@@ -921,9 +949,13 @@ Plan make_plan(uint32_t M, uint32_t N, uint32_t K, uint32_t splits_req, int num_
         return e ? atoi(e) : 0;
     }();
     if (p.pair && N % 512 == 0 && pair_bn_env != 256) {
+        // costs in half 256 x 256 tile-times: a wide tile ~3, a 256 x 256 tile 2; a wide tail of at most half the
+        // SM pairs runs as 256-column slices (one 256 x 256 wave)
         const uint64_t pairs = (uint64_t)num_sms / 2, rows = (M + 255) / 256;
-        const uint64_t w256 = (rows * p.tiles_n + pairs - 1) / pairs, w512 = (rows * (N / 512) + pairs - 1) / pairs;
-        if (pair_bn_env == 512 || (p.k_blocks >= 32 && 3 * w512 <= 2 * w256)) {
+        const uint64_t t512 = rows * (N / 512), tail = t512 % pairs;
+        const uint64_t c256 = 2 * ((rows * p.tiles_n + pairs - 1) / pairs);
+        const uint64_t c512 = 3 * (t512 / pairs) + (tail == 0 ? 0 : (2 * tail <= pairs ? 2 : 3));
+        if (pair_bn_env == 512 || (p.k_blocks >= 32 && c512 <= c256)) {
             p.pair_bn = 512;
             p.tiles_n = N / 512;
         }
@@ -957,7 +989,16 @@ int launch_pair(const Plan &p, const CUtensorMap &mx, const CUtensorMap &mw, con
     }
     a.num_tiles = ((a.M + 255) / 256) * p.tiles_n;
     a.splits = 1;
-    const uint32_t pairs = min(a.num_tiles, (uint32_t)sh::state().num_sms / 2);
+    const uint32_t sm_pairs = (uint32_t)sh::state().num_sms / 2;
+    a.full_units = a.num_units = a.num_tiles;
+    if (BN > (int)PairCfg<BN>::kMmaN) {   // wide tiles: a last wave at most half full runs as column slices
+        const uint32_t full = (a.num_tiles / sm_pairs) * sm_pairs, tail = a.num_tiles - full;
+        if (tail && tail * (BN / PairCfg<BN>::kMmaN) <= sm_pairs) {
+            a.full_units = full;
+            a.num_units = full + tail * (BN / PairCfg<BN>::kMmaN);
+        }
+    }
+    const uint32_t pairs = min(a.num_units, sm_pairs);
     return sh::cuda_ok(sh::launch_pdl(k_gemm_tc2<BN>, dim3(2 * pairs), dim3(kPairThreads), PairCfg<BN>::kSmem, st, mx,
                                   mw, mz, a),
                        "sh_gemm launch (pair)")

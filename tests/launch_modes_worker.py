@@ -1,6 +1,6 @@
 """Runs a small encoder forward (2 SigLIP-base layers, B = 12: 2-CTA and 1-CTA GEMMs, tcgen05 attention, LayerNorm),
-one wide GEMM (2816 x 4096 x 256: 11 x 16 pair tiles, a partial tile group) and one long-K GEMM (4096 x 4096 x 2048:
-256 x 512 pair tiles) on GPU 0 and prints the SHA-1 of their output bytes. tests/test_launch_modes_gpu.py runs it
+one wide GEMM (2816 x 4096 x 256: 11 x 16 pair tiles, a partial tile group) and two long-K GEMMs (4096 x 4096 x
+2048: 256 x 512 pair tiles; 8192 x 4096 x 2048: the same with a tail wave of column slices) on GPU 0 and prints the SHA-1 of their output bytes. tests/test_launch_modes_gpu.py runs it
 under different launch settings (SH_PDL, SH_GEMM_GROUP_M, SH_GEMM_PAIR_BN), which are read once per process, and
 requires identical bytes: the launch mode, the tile order and the tile width must not change any result."""
 from __future__ import annotations
@@ -54,8 +54,17 @@ def main():
         raise RuntimeError(lib.sh_cuda_last_error_string().decode())
     rt.check()
     wide = rt.get(z2, M2, N2)
+    # 8192 x 4096 x 2048: 256 wide tiles, the last 34 as 68 column slices (SH_GEMM_PAIR_BN=256: 512 narrow tiles)
+    M3, N3, K3 = 8192, 4096, 2048
+    a3, w3, z3 = rt.alloc(M3, K3), rt.alloc(K3, N3), rt.alloc(M3, N3)
+    lib.sh_test_fill_fp16(a3, M3, K3, K3, 7, -1024, 1023, 1.0 / 1024)
+    lib.sh_test_fill_fp16(w3, K3, N3, N3, 8, -1024, 1023, 1.0 / 1024)
+    if lib.sh_cuda_gemm(a3, w3, z3, M3, N3, K3, K3, N3, N3, 0, 0, N3, 0, 0):
+        raise RuntimeError(lib.sh_cuda_last_error_string().decode())
+    rt.check()
+    tail = rt.get(z3, M3, N3)
     h = lambda t: hashlib.sha1(np.ascontiguousarray(t).view(np.uint8).tobytes()).hexdigest()  # noqa: E731
-    print(f"HASH {h(enc)} {h(gem)} {h(wide)}", flush=True)
+    print(f"HASH {h(enc)} {h(gem)} {h(wide)} {h(tail)}", flush=True)
 
 
 if __name__ == "__main__":

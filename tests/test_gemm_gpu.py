@@ -212,10 +212,12 @@ def test_pair_tiles(gpu_lib, M, N, K, flags):
     _close(got, want, K)
 
 
-# Shapes the planner gives 256 x 512 pair tiles (N % 512 == 0, K >= 2048, and 1.5 x the wide waves <= the 256 x 256
-# waves on 74 SM pairs): 4096 x 4096 (4 vs 2 waves), 2816 x 2048 (11 row-tiles, ragged; 2 vs 1), 4096 x 2048 (2 vs 1).
+# Shapes the planner gives 256 x 512 pair tiles (N % 512 == 0, K >= 2048, and cheaper waves on 74 SM pairs):
+# 4096 x 4096, 2816 x 2048 (11 row-tiles, ragged), 4096 x 2048; 8192 / 8000 x 4096 have 256 wide tiles, 3 full waves
+# and a tail of 34 that runs as 68 256-column slices.
 @pytest.mark.parametrize("M,N,K,flags", [(4096, 4096, 2048, 0), (2816, 2048, 4096, L.EPI_BIAS | L.EPI_RESIDUAL),
-                                         (4096, 2048, 2048, L.EPI_ACCUMULATE | L.EPI_BIAS)])
+                                         (4096, 2048, 2048, L.EPI_ACCUMULATE | L.EPI_BIAS),
+                                         (8192, 4096, 2048, L.EPI_BIAS | L.EPI_RESIDUAL), (8000, 4096, 2048, 0)])
 def test_wide_pair_tiles(gpu_lib, M, N, K, flags):
     got, want = _run(gpu_lib, M, N, K, flags=flags)
     _close(got, want, K)
