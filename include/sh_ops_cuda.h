@@ -57,6 +57,22 @@ uint32_t sh_cuda_abi_version(void);                 /* 1 */
 int sh_cuda_gemm(uint64_t x, uint64_t w, uint64_t z, uint32_t M, uint32_t N, uint32_t K, uint32_t ldx, uint32_t ldw,
                  uint32_t ldz, uint64_t bias, uint64_t residual, uint32_t ldr, uint32_t flags, uint32_t splits);
 
+/* ---- the GEMM planner as a query ---------------------------------------------------------------------------------
+ * No counterpart in the reference. The kernel and tiling sh_cuda_gemm picks for 16-byte-aligned operands of an
+ * M x N x K product with `splits` as in sh_cuda_gemm, on a GPU with `num_sms` SMs (0: the current device's; any
+ * other value makes no CUDA call, so the query runs without a GPU):
+ *   kernel      0 CUDA-core fallback (K == 0), 1 single-CTA tcgen05 (128 x bn tiles), 2 two-CTA tcgen05 (256 x bn)
+ *   k_blocks    64-deep K blocks; splits: K pieces per tile (split-K, single-CTA kernel only)
+ *   units       work units of the launch: tiles x splits, or for kernel 2 whole tiles below full_units and
+ *               256-column slices of the remaining tiles past it (a short last wave of 256 x 512 tiles)
+ *   grid        CTAs launched
+ * Returns 0, or -1 when out is NULL. */
+typedef struct sh_cuda_gemm_plan_t {
+    uint32_t kernel, bn, tiles_m, tiles_n, k_blocks, splits, full_units, units, grid;
+} sh_cuda_gemm_plan_t;
+int sh_cuda_gemm_plan(uint32_t M, uint32_t N, uint32_t K, uint32_t splits, uint32_t num_sms,
+                      sh_cuda_gemm_plan_t *out);
+
 /* ---- GEMM with LayerNorm folded in, and row statistics out ----------------------------------------------------------
  * No counterpart in the reference: the library form of "layernorm -> gemm" (frontend/siglip.py:136-162) without
  * materialising the normalised rows. With W' = diag(gamma) W, colsum = 1^T W' (fp32, 1 x N) and

@@ -19,6 +19,7 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <algorithm>
 #include <mutex>
 #include <utility>
 
@@ -975,6 +976,24 @@ int launch_tc(const Plan &p, const CUtensorMap &mx, const CUtensorMap &mw, const
                : -1;
 }
 
+// Work units of the 2-CTA kernel (pair_unit): whole tiles, except that a last wave of wide tiles filling at most
+// half the SM pairs runs as 256-column slices, bn / 256 units per tile.
+struct PairUnits {
+    uint32_t full, units;
+};
+PairUnits pair_units(uint32_t num_tiles, uint32_t bn, uint32_t sm_pairs) {
+    PairUnits r{num_tiles, num_tiles};
+    const uint32_t nh = bn > 256 ? bn / 256 : 1;
+    if (nh > 1 && sm_pairs > 0) {
+        const uint32_t full = (num_tiles / sm_pairs) * sm_pairs, tail = num_tiles - full;
+        if (tail && tail * nh <= sm_pairs) {
+            r.full = full;
+            r.units = full + tail * nh;
+        }
+    }
+    return r;
+}
+
 template <int BN>
 int launch_pair(const Plan &p, const CUtensorMap &mx, const CUtensorMap &mw, const CUtensorMap &mz, GemmArgs a,
                 cudaStream_t st) {
@@ -990,14 +1009,9 @@ int launch_pair(const Plan &p, const CUtensorMap &mx, const CUtensorMap &mw, con
     a.num_tiles = ((a.M + 255) / 256) * p.tiles_n;
     a.splits = 1;
     const uint32_t sm_pairs = (uint32_t)sh::state().num_sms / 2;
-    a.full_units = a.num_units = a.num_tiles;
-    if (BN > (int)PairCfg<BN>::kMmaN) {   // wide tiles: a last wave at most half full runs as column slices
-        const uint32_t full = (a.num_tiles / sm_pairs) * sm_pairs, tail = a.num_tiles - full;
-        if (tail && tail * (BN / PairCfg<BN>::kMmaN) <= sm_pairs) {
-            a.full_units = full;
-            a.num_units = full + tail * (BN / PairCfg<BN>::kMmaN);
-        }
-    }
+    const PairUnits pu = pair_units(a.num_tiles, BN, sm_pairs);
+    a.full_units = pu.full;
+    a.num_units = pu.units;
     const uint32_t pairs = min(a.num_units, sm_pairs);
     return sh::cuda_ok(sh::launch_pdl(k_gemm_tc2<BN>, dim3(2 * pairs), dim3(kPairThreads), PairCfg<BN>::kSmem, st, mx,
                                   mw, mz, a),
@@ -1226,6 +1240,35 @@ int sh_cuda_gemm(uint64_t x, uint64_t w, uint64_t z, uint32_t M, uint32_t N, uin
                  uint32_t ldz, uint64_t bias, uint64_t residual, uint32_t ldr, uint32_t flags, uint32_t splits) {
     return sh::gemm_run(x, w, z, M, N, K, ldx, ldw, ldz, bias, residual, ldr, flags, splits, "sh_cuda_gemm",
                         nullptr);
+}
+
+int sh_cuda_gemm_plan(uint32_t M, uint32_t N, uint32_t K, uint32_t splits, uint32_t num_sms,
+                      sh_cuda_gemm_plan_t *out) {
+    if (!out) return -1;
+    *out = sh_cuda_gemm_plan_t{};
+    if (M == 0 || N == 0) return 0;
+    const uint32_t sms = num_sms ? num_sms : (uint32_t)sh::state().num_sms;
+    if (K == 0 || sms == 0) return 0;   // the CUDA-core kernel
+    const Plan p = make_plan(M, N, K, splits, (int)sms);
+    out->k_blocks = p.k_blocks;
+    out->splits = p.splits;
+    out->tiles_n = p.tiles_n;
+    if (p.pair) {
+        out->kernel = 2;
+        out->bn = (uint32_t)p.pair_bn;
+        out->tiles_m = (M + 255) / 256;
+        const PairUnits pu = pair_units(out->tiles_m * p.tiles_n, out->bn, sms / 2);
+        out->full_units = pu.full;
+        out->units = pu.units;
+        out->grid = 2 * std::min(pu.units, sms / 2);
+    } else {
+        out->kernel = 1;
+        out->bn = (uint32_t)p.bn;
+        out->tiles_m = p.tiles_m;
+        out->units = out->full_units = p.tiles_m * p.tiles_n * p.splits;
+        out->grid = std::min(out->units, sms);
+    }
+    return 0;
 }
 
 int sh_cuda_gemm_ln(uint64_t x, uint64_t w, uint64_t z, uint32_t M, uint32_t N, uint32_t K, uint32_t ldx,

@@ -23,6 +23,12 @@ class GemmCfg(C.Structure):
 
 
 CFG_P = C.POINTER(GemmCfg)
+
+
+class GemmPlan(C.Structure):
+    """sh_cuda_gemm_plan_t (include/sh_ops_cuda.h): the planner's choice for one GEMM shape."""
+    _fields_ = [(n, u32) for n in ("kernel", "bn", "tiles_m", "tiles_n", "k_blocks", "splits", "full_units",
+                                   "units", "grid")]
 FN_VOID = C.CFUNCTYPE(None)
 
 # name: (restype, [argtypes]) -- one entry per declaration in include/*.h
@@ -73,6 +79,7 @@ SIGNATURES: dict[str, tuple] = {
     "sh_cuda_last_error": (i32, []), "sh_cuda_last_error_string": (cp, []), "sh_cuda_device_error": (i32, []),
     "sh_cuda_num_sms": (i32, []), "sh_cuda_timer_last_ms": (f32, []), "sh_cuda_abi_version": (u32, []),
     "sh_cuda_gemm": (i32, [u64, u64, u64, u32, u32, u32, u32, u32, u32, u64, u64, u32, u32, u32]),
+    "sh_cuda_gemm_plan": (i32, [u32, u32, u32, u32, u32, C.POINTER(GemmPlan)]),
     "sh_cuda_gemm_ln": (i32, [u64, u64, u64, u32, u32, u32, u32, u32, u32, u64, u64, u32, u32, u64, u64, f32, u64]),
     "sh_rmsnorm": (None, [u64, u64, u64, u32, u32, u32, f32, u32]),
     "sh_rope": (None, [u64, u64, u64, u32, u32, u32, u32, u32, u32]),
