@@ -391,10 +391,4 @@ __device__ __forceinline__ float gelu_fast(float x) {
     return fmaf(hx, t, hx);
 }
 
-__device__ __forceinline__ float gelu_tanh(float x) {
-    // 0.5 x (1 + tanh(u)) with u = sqrt(2/pi) (x + 0.044715 x^3), written as x * sigmoid(2u)
-    const float u2 = 1.5957691216057308f * (x + 0.044715f * x * x * x);
-    return x / (1.0f + __expf(-u2));
-}
-
 #endif  // __CUDACC__
