@@ -483,6 +483,16 @@ def run_ours(args, rank: int, world: int, local: int) -> dict | None:
 
 
 # ---- the CPU leg: the reference's numpy layer (oracle port) ------------------------------------------------------------
+def host_blas() -> str:
+    """The BLAS numpy runs the CPU baselines on (name, version and build configuration)."""
+    try:
+        import numpy as np
+        b = np.__config__.CONFIG["Build Dependencies"]["blas"]
+        return f"{b.get('name', '?')} {b.get('version', '?')} ({b.get('openblas configuration', '').strip()})"
+    except Exception:   # a numpy without the build-config table
+        return "unknown"
+
+
 def cpu_layer_setup(seed: int = 3):
     import numpy as np
     from oracle import lcg, siglip
@@ -500,7 +510,7 @@ def cpu_baseline(images: int) -> dict:
         for _ in range(NLAYERS):
             cur = siglip.layer_reference_arrays(cur, p, H)["OUT"]
     dt = time.perf_counter() - t0
-    return {"value": round(images / dt, 4), "unit": "images/s", "cores": os.cpu_count(), "kind": "port",
+    return {"value": round(images / dt, 4), "unit": "images/s", "cores": os.cpu_count(), "blas": host_blas(), "kind": "port",
             "sample": f"{images} image(s) x {NLAYERS} layers (S={S}, D={D}) of the 512-image batch through the numpy "
                       f"oracle of siglip_ref.layer_reference (fp32 BLAS, all host threads); {dt:.1f} s"}
 
@@ -526,7 +536,7 @@ def run_reference(args, rank: int, world: int) -> dict | None:
             "data": "synthetic (seeded LCG)", "impl": "reference",
             "config": {"workload": "SigLIP-base 12-layer encoder forward (BASELINE config 5)",
                        "global_batch": GLOBAL_BATCH, "seq_len": S, "parallelism": "cpu"},
-            "cpu_baseline": {"value": round(value, 4), "unit": "images/s", "cores": os.cpu_count(), "kind": "port",
+            "cpu_baseline": {"value": round(value, 4), "unit": "images/s", "cores": os.cpu_count(), "blas": host_blas(), "kind": "port",
                              "sample": sample},
             "e2e": {"value": round(value, 4), "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
@@ -916,7 +926,7 @@ def summa_cpu_baseline(n: int, sample: int = 4096) -> dict:
     a @ b
     dt = time.perf_counter() - t0
     tf = 2.0 * sample ** 3 / dt / 1e12
-    return {"value": round(tf, 4), "unit": "TFLOP/s", "cores": os.cpu_count(), "kind": "port",
+    return {"value": round(tf, 4), "unit": "TFLOP/s", "cores": os.cpu_count(), "blas": host_blas(), "kind": "port",
             "sample": f"one fp32 {sample}^3 numpy matmul ({dt:.2f} s); the {n}^3 product at that rate would take "
                       f"{2.0 * n ** 3 / tf / 1e12:.0f} s"}
 
