@@ -1,7 +1,7 @@
 """Generate the golden fixtures in this folder from the reference's own Python modules.
 
-Run where a checkout of runwangdl/softhier-mlir is available (default: the path in the
-SOFTHIER_REF environment variable, else /root/reference):
+Run where a checkout of runwangdl/softhier-mlir is available; set SOFTHIER_REF to its path (the default is where
+the build environment mounts it):
 
     python tests/golden/make_golden.py
 
