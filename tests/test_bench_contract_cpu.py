@@ -24,3 +24,31 @@ def test_reference_arm_prints_one_contract_line():
     assert d["cpu_baseline"]["value"] == d["value"] and d["cpu_baseline"]["kind"] in ("port", "reference")
     assert d["cpu_baseline"]["cores"] >= 1 and d["cpu_baseline"]["sample"] and d["cpu_baseline"]["blas"]
     assert d["e2e"] == {"value": d["value"], "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+
+
+def _bench_module():
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("bench_under_test", ROOT / "bench.py")
+    m = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(m)
+    return m
+
+
+def test_roofline_traffic_comes_from_the_committed_profile():
+    b = _bench_module()
+    t = b.profile_traffic("gemm_fc1_m131072")        # the default workload's FC1 launch (B = 512 x S = 256 rows)
+    assert t is not None and 0.5e9 < t < 2e9
+    assert b.profile_traffic("no_such_kernel") is None
+
+
+def test_clock_summary_reads_nvml_samples():
+    b = _bench_module()
+    c = b.ClockSampler(0)
+    c.nvml = type("FakeNvml", (), {"nvmlShutdown": staticmethod(lambda: None)})
+    c.thread = type("T", (), {"join": lambda self, timeout=None: None})()
+    c.samples = [(1965.0, 1965.0, 0)]                 # before the timed region: dropped by mark()
+    c.mark()
+    c.samples += [(1400.0, 1965.0, 0x4), (1420.0, 1965.0, 0x4), (1380.0, 1965.0, 0x4 | 0x40)]
+    got = c.stop()
+    assert got["sm_mhz"] == 1400.0 and got["sm_max_mhz"] == 1965.0 and got["samples"] == 3
+    assert got["reasons"] == ["hw_thermal_slowdown", "sw_power_cap"]
