@@ -2,19 +2,25 @@
 // (reference: runtime/sh_gemm.inc.c:17-117 sh_cfg_fill / sh_gemm_l1_bytes / sh_gemm, :127-189 sh_gemm_mesh,
 // :192-344 sh_gemm_xmcast_ex; declared at runtime/sh_ops.h:54-88).
 //
-// The reference streams tm x tk / tk x tn tiles into TCDM and accumulates on RedMulE. Here one persistent CTA per
-// SM runs a warp-specialised tcgen05 pipeline:
-//   warp 0    TMA producer: X tile [128 x 64] (K-major) and W tile [64 x BN] (N-major, i.e. W as stored) per
-//             stage into a multi-stage ring of 128-byte-swizzled shared memory, completion on mbarriers;
-//   warp 1    MMA issuer: one thread issues tcgen05.mma (M=128, N=BN, K=16) into one of two TMEM accumulators
-//             and tcgen05.commit frees each stage / publishes each finished accumulator;
-//   warps 2-5 epilogue: tcgen05.ld the accumulator (each warp owns its 32-lane quarter = 32 rows), apply the
-//             fused epilogue (accumulate / bias / GELU / residual) and store fp16; the second accumulator lets the
-//             next tile's MMAs run meanwhile.
-// Split-K ("K-accumulation" across CTAs) writes fp32 partial tiles to a workspace; the last CTA to finish a tile
-// (arrival counter) sums the partials in split order and runs the epilogue, then resets the counter.
+// The reference streams tm x tk / tk x tn tiles into TCDM and accumulates on RedMulE. Here persistent CTAs (one
+// per SM, or one cluster of two per SM pair) run a warp-specialised tcgen05 pipeline:
+//   warp 0     TMA producer: X tile [128 x 64] (K-major) and W tiles [64 x 64] (N-major, i.e. W as stored) per
+//              stage into a ring of 128-byte-swizzled shared memory, completion on mbarriers;
+//   warp 1     MMA issuer: one thread issues tcgen05.mma into a tensor-memory accumulator; tcgen05.commit frees
+//              each stage and publishes each finished accumulator;
+//   warps 2-9  epilogue: tcgen05.ld the accumulator (warp w owns TMEM lane quarter w % 4 = 32 rows, and half of
+//              the columns), apply the fused epilogue (accumulate / bias / GELU / residual / fp32 in or out) and
+//              write fp16 through 32 x 32 staging tiles and TMA stores.
+// k_gemm_tc<BN>: single CTA, 128 x BN tiles, two accumulators (the next tile's MMAs run while the epilogue drains),
+//   split-K: fp32 partial tiles in a workspace, the last CTA of a tile (arrival counter) sums them in split order.
+// k_gemm_tc2<BN>: a cluster of two CTAs, tcgen05.mma.cta_group::2 (M = 256), each CTA loading its half of the W
+//   columns; BN = 256 with two accumulators, or BN = 512 (two N = 256 MMAs per k-step, one accumulator, 25 % fewer
+//   operand bytes per MAC) for long K loops, whose short last wave may run as 256-column slices (pair_unit).
+// Tiles are taken in groups of row-tiles (tile_coords) so that concurrent CTAs share X and W in L2, and every launch
+// uses programmatic dependent launch (set-up overlaps the previous kernel). The planner (make_plan, queryable as
+// sh_cuda_gemm_plan) picks the kernel and tiling per shape.
 // Every mbarrier wait is bounded (SH_SPIN_CYCLES): on a timeout the CTA raises the device error word, skips its
-// remaining work, waits for its outstanding TMA loads and frees its tensor memory.
+// remaining work, waits for its outstanding TMA loads and MMAs and frees its tensor memory.
 // Shapes the TMA path cannot address (16-byte alignment of base or leading dimension) use a CUDA-core kernel.
 #include <stdlib.h>
 #include <string.h>
