@@ -1301,6 +1301,10 @@ int sh_cuda_gemm_ln(uint64_t x, uint64_t w, uint64_t z, uint32_t M, uint32_t N, 
 // device current) and should therefore come before any stream capture on it. Every call shares the array and
 // clears the counters it uses before its kernel, on the caller's stream: calls that overlap on the GPU (two
 // streams, two threads) race on the array and must be serialised by the caller.
+// It always runs the single-CTA kernel (the only one with a split-K path), so the planner's 2-CTA choice is
+// replaced by 128 x BN tiles. Stream: the one bound with sh_cuda_set_stream once the runtime has started on the
+// device, else the legacy default stream; a kernel's bounded-wait error then lands in the array's error word,
+// which sh_cuda_device_error also reads and clears.
 // ================================================================================================================
 namespace {
 
@@ -1331,14 +1335,43 @@ void *noalloc_scratch(int dev) {
 
 }  // namespace
 
+namespace sh {
+
+// Returns and clears the no-alloc array's error word on `dev` (the current device); 0 when no call has looked
+// the array up there. Used by sh_cuda_device_error after its stream synchronisation.
+int noalloc_take_error(int dev) {
+    if (dev < 0 || dev >= kMaxDevices) return 0;
+    void *base = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(g_scratch_mu);
+        base = g_scratch_addr[dev];
+    }
+    if (!base) return 0;
+    int v = 0;
+    int *word = reinterpret_cast<int *>(static_cast<unsigned char *>(base) + kNoAllocErrOffset);
+    if (!cuda_ok(cudaMemcpy(&v, word, sizeof v, cudaMemcpyDeviceToHost), "sh_cuda_device_error")) return -1;
+    if (v) cudaMemset(word, 0, sizeof(int));
+    return v;
+}
+
+}  // namespace sh
+
 extern "C" int sh_cuda_gemm_splitk_noalloc(uint64_t x, uint64_t w, uint64_t z, uint32_t M, uint32_t N, uint32_t K,
                                            uint32_t ldx, uint32_t ldw, uint32_t ldz, uint64_t bias, uint64_t residual,
                                            uint32_t ldr, uint32_t flags, uint32_t splits) {
     const char *name = "sh_cuda_gemm_splitk_noalloc";
+    constexpr uint32_t kFlags = SH_EPI_ACCUMULATE | SH_EPI_BIAS | SH_EPI_GELU | SH_EPI_RESIDUAL | SH_EPI_F32_OUT |
+                                SH_EPI_ACC_F32_IN | SH_GEMM_SIMT;
+    if (flags & ~kFlags) {
+        sh::set_error(-1, "[%s] flags %#x: only accumulate / bias / gelu / residual / fp32 out / fp32 carry-in / "
+                          "simt are supported", name, flags);
+        return -1;
+    }
     if (M == 0 || N == 0) return 0;
     if (!x || !w || !z || ldx < K || ldw < N || ldz < N || ((flags & SH_EPI_BIAS) && !bias) ||
-        ((flags & SH_EPI_RESIDUAL) && (!residual || ldr < N))) {
-        sh::set_error(-1, "[%s] bad operands: %ux%ux%u ld %u/%u/%u", name, M, N, K, ldx, ldw, ldz);
+        ((flags & (SH_EPI_RESIDUAL | SH_EPI_ACC_F32_IN)) && (!residual || ldr < N)) ||
+        ((flags & SH_EPI_RESIDUAL) && (flags & SH_EPI_ACC_F32_IN))) {
+        sh::set_error(-1, "[%s] bad operands: %ux%ux%u ld %u/%u/%u flags %#x", name, M, N, K, ldx, ldw, ldz, flags);
         return -1;
     }
     int dev = 0;
@@ -1364,12 +1397,12 @@ extern "C" int sh_cuda_gemm_splitk_noalloc(uint64_t x, uint64_t w, uint64_t z, u
     a.K = K;
     a.ldz = ldz;
     a.ldr = ldr;
-    a.flags = flags & (SH_EPI_ACCUMULATE | SH_EPI_BIAS | SH_EPI_GELU | SH_EPI_RESIDUAL);
+    a.flags = flags & ~(uint32_t)SH_GEMM_SIMT;
     a.err = bound_err ? bound_err : reinterpret_cast<int *>(scratch + kNoAllocErrOffset);
     a.vec = sh::aligned16(z) && ldz % 8 == 0 && (!(flags & SH_EPI_BIAS) || sh::aligned16(bias)) &&
-            (!(flags & SH_EPI_RESIDUAL) || (sh::aligned16(residual) && ldr % 8 == 0));
-    const bool tc = K > 0 && sh::aligned16(x) && sh::aligned16(w) && ldx % 8 == 0 && ldw % 8 == 0 &&
-                    sh::encode_tiled() != nullptr;
+            (!(flags & (SH_EPI_RESIDUAL | SH_EPI_ACC_F32_IN)) || (sh::aligned16(residual) && ldr % 8 == 0));
+    const bool tc = !(flags & SH_GEMM_SIMT) && K > 0 && sh::aligned16(x) && sh::aligned16(w) && ldx % 8 == 0 &&
+                    ldw % 8 == 0 && sh::encode_tiled() != nullptr;
     if (!tc) {   // the CUDA-core kernel needs no scratch
         dim3 grid((N + 63) / 64, (M + 63) / 64);
         if (grid.y > 65535u) {
@@ -1380,6 +1413,11 @@ extern "C" int sh_cuda_gemm_splitk_noalloc(uint64_t x, uint64_t w, uint64_t z, u
         return sh::cuda_ok(cudaGetLastError(), name) ? 0 : -1;
     }
     Plan p = make_plan(M, N, K, splits, num_sms);
+    if (p.pair) {   // 256 x 512 pair tiles set tiles_n = N / 512; this entry point launches 128 x bn tiles
+        p.pair = false;
+        p.pair_bn = 256;
+        p.tiles_n = (N + p.bn - 1) / p.bn;
+    }
     a.tiles_n = p.tiles_n;
     a.group_m = gemm_group_m();
     a.num_tiles = p.tiles_m * p.tiles_n;

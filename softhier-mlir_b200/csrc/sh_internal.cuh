@@ -54,6 +54,7 @@ inline cudaStream_t stream() { return state().stream; }
 // The stream bound with sh_cuda_set_stream and the kernels' error word, if the device's state already exists;
 // never initialises it (so never allocates). nullptr / the legacy default stream otherwise.
 cudaStream_t peek_stream(int device, int **dev_err);
+int noalloc_take_error(int device);    // sh_cuda_gemm_splitk_noalloc's error word (sh_gemm.cu), read and cleared
 float *workspace(size_t bytes);       // grows the split-K workspace (not during stream capture)
 uint32_t *tile_counters(size_t n);
 

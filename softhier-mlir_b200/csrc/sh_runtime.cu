@@ -424,12 +424,15 @@ const char *sh_cuda_last_error_string(void) { return t_err_msg; }
 
 int sh_cuda_device_error(void) {
     DeviceState &s = state();
-    if (!s.dev_err) return 0;
     int v = 0;
     if (!cuda_ok(cudaStreamSynchronize(s.stream), "sh_cuda_device_error")) return -1;
-    if (!cuda_ok(cudaMemcpy(&v, s.dev_err, sizeof v, cudaMemcpyDeviceToHost), "sh_cuda_device_error")) return -1;
-    if (v) cudaMemset(s.dev_err, 0, sizeof(int));
-    return v;
+    if (s.dev_err) {
+        if (!cuda_ok(cudaMemcpy(&v, s.dev_err, sizeof v, cudaMemcpyDeviceToHost), "sh_cuda_device_error")) return -1;
+        if (v) cudaMemset(s.dev_err, 0, sizeof(int));
+    }
+    // kernels of sh_cuda_gemm_splitk_noalloc launched before the runtime started report into its fixed array
+    const int nv = noalloc_take_error(s.device);
+    return v ? v : nv;
 }
 
 int sh_cuda_num_sms(void) { return state().num_sms; }
