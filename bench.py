@@ -222,28 +222,10 @@ class ClockSampler:
 
 # ---- the GPU arm -----------------------------------------------------------------------------------------------------
 def setup_encoder(rt, B: int, rank: int, nlayers: int = NLAYERS):
-    """Device weights (identical on every rank) and activations for a shard of B sequences."""
+    """Device weights (identical on every rank) and activations for a shard of B sequences: the library's synthetic
+    encoder (softhier_cuda.encoder.synthetic_encoder), input seed 100 + rank."""
     from softhier_cuda import encoder
-    lib = rt.lib
-    layers = []
-    for li in range(nlayers):
-        a = rt.alloc
-        w = encoder.LayerWeights(wqkv=a(D, 3 * D), bqkv=a(1, 3 * D), wo=a(D, D), bo=a(1, D), w1=a(D, F), b1=a(1, F),
-                                 w2=a(F, D), b2=a(1, D), g1=a(1, D), be1=a(1, D), g2=a(1, D), be2=a(1, D))
-        seed = 7000 + 16 * li
-        lib.sh_cuda_fill_normal_fp16(w.wqkv, D, 3 * D, 3 * D, seed + 0, 0.0, 0.02)
-        lib.sh_cuda_fill_normal_fp16(w.wo, D, D, D, seed + 1, 0.0, 0.02)
-        lib.sh_cuda_fill_normal_fp16(w.w1, D, F, F, seed + 2, 0.0, 0.02)
-        lib.sh_cuda_fill_normal_fp16(w.w2, F, D, D, seed + 3, 0.0, 0.02)
-        for b, n in ((w.bqkv, 3 * D), (w.bo, D), (w.b1, F), (w.b2, D), (w.be1, D), (w.be2, D)):
-            lib.sh_test_fill_const_fp16(b, 1, n, n, 0x0000)
-        for g in (w.g1, w.g2):
-            lib.sh_test_fill_const_fp16(g, 1, D, D, 0x3C00)
-        layers.append(w)
-    act = encoder.alloc_activations(rt, B, S, D, F)
-    x_in = rt.alloc(B * S, D)
-    lib.sh_cuda_fill_normal_fp16(x_in, B * S, D, D, 100 + rank, 0.0, 1.0)
-    return layers, act, x_in
+    return encoder.synthetic_encoder(rt, B, S, D, F, nlayers, encoder.INPUT_SEED0 + rank)
 
 
 def schedule_maker(rt, act, layers, M: int, fold: bool):

@@ -15,8 +15,8 @@
  *  - constraint violations return <0 and print one "[sh_...] reason" line, exactly as the reference does;
  *    asynchronous CUDA failures are reported by sh_cuda_last_error() (sh_ops_cuda.h). Nothing aborts the
  *    process or traps the device.
- * Reference symbols outside the hot path (sh_l1_*, sh_redmule, sh_dma_*, sh_x_*, sh_t_*, sh_f_*, sh_wm_*,
- * the sh_llm ops) are not exported by this library.
+ * Reference symbols outside the hot path (sh_l1_*, sh_redmule, sh_dma_*, sh_x_*, sh_t_*, sh_f_*, sh_wm_*)
+ * are not exported by this library. The sh_llm decoder ops (sh_ops.h:277-303) are, and are declared below.
  */
 #ifndef SH_OPS_H
 #define SH_OPS_H

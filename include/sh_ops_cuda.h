@@ -121,9 +121,14 @@ int sh_cuda_attention_batched(uint64_t q, uint64_t k, uint64_t v, uint64_t o, ui
 
 /* ---- synthetic inputs -------------------------------------------------------------------------------------------
  * N(mean, std) fp16 from the LCG of sh_test_fill_fp16: per element two draws d0, d1, u = (d + 0.5) / 2^24 and
- * Box-Muller z = sqrt(-2 ln u0) cos(2 pi u1) in fp32, on the device. */
+ * Box-Muller z = sqrt(-2 ln u0) cos(2 pi u1), with ln and cos evaluated as fixed series of correctly rounded fp32
+ * operations (no library math, no FMA contraction), so every implementation of the definition gives the same bits.
+ * sh_cuda_fill_normal_fp16 fills device memory on the library stream; sh_cuda_host_fill_normal_fp16 fills host
+ * memory (fp16 codes) on the calling CPU thread and needs no GPU. */
 void sh_cuda_fill_normal_fp16(uint64_t a, uint32_t rows, uint32_t cols, uint32_t ld, uint32_t seed, float mean,
                               float stdev);
+void sh_cuda_host_fill_normal_fp16(uint16_t *dst, uint32_t rows, uint32_t cols, uint32_t ld, uint32_t seed,
+                                   float mean, float stdev);
 
 /* ---- LCG sub-block fill (2-D block-distributed inputs) -----------------------------------------------------------
  * Fill rows x cols (leading dim ld) with elements [row0 .., col0 ..] of the global gcols-wide matrix that

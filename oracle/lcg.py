@@ -15,7 +15,8 @@ golden vectors in tests/golden pin that.
 `uniform_fp16` / `normal_fp16` are the input distributions BASELINE asks for. Uniform is
 exactly `fill_fp16(.., -1024, 1023, 1/1024)` (reference semantics); the normal generator is an
 EXTENSION defined by this repository (the reference's LCG only yields scaled integers):
-Box-Muller over consecutive draw pairs, float64 math, RNE to fp16.
+Box-Muller over consecutive draw pairs with ln / cos as fixed series of correctly rounded
+float32 operations, RNE to fp16 - a definition every implementation reproduces bit for bit.
 """
 from __future__ import annotations
 
@@ -34,12 +35,27 @@ def _compose(a1: int, c1: int, a2: int, c2: int) -> tuple[int, int]:
     return (a2 * a1) & _MASK, (a2 * c1 + c2) & _MASK
 
 
-def lcg_states(seed: int, n: int) -> np.ndarray:
-    """The n successive 32-bit LCG states after seeding (state_1 .. state_n), uint32."""
+def _jump(n: int) -> tuple[int, int]:
+    """The affine map (a, c) that advances a state by n steps (square-and-multiply)."""
+    acc, p = (1, 0), (LCG_A, LCG_C)
+    while n:
+        if n & 1:
+            acc = _compose(acc[0], acc[1], p[0], p[1])
+        p = _compose(p[0], p[1], p[0], p[1])
+        n >>= 1
+    return acc
+
+
+def lcg_states(seed: int, n: int, skip: int = 0) -> np.ndarray:
+    """The n successive 32-bit LCG states after seeding (state_1 .. state_n), uint32; with `skip`, the states
+    state_{skip+1} .. state_{skip+n} (the stream jumped ahead by `skip` draws)."""
     out = np.empty(n, dtype=np.uint32)
     if n == 0:
         return out
     s0 = (int(seed) ^ SEED_XOR) & _MASK
+    if skip:
+        a, c = _jump(int(skip))
+        s0 = (a * s0 + c) & _MASK
     out[0] = (s0 * LCG_A + LCG_C) & _MASK
     filled = 1
     step_a, step_c = LCG_A, LCG_C           # map advancing a state by `filled` steps
@@ -52,9 +68,9 @@ def lcg_states(seed: int, n: int) -> np.ndarray:
     return out
 
 
-def lcg_draws(seed: int, n: int) -> np.ndarray:
-    """The n successive draws (state >> 8) of the device LCG, uint32 in [0, 2**24)."""
-    return lcg_states(seed, n) >> np.uint32(8)
+def lcg_draws(seed: int, n: int, skip: int = 0) -> np.ndarray:
+    """The n successive draws (state >> 8) of the device LCG, uint32 in [0, 2**24), after `skip` draws."""
+    return lcg_states(seed, n, skip) >> np.uint32(8)
 
 
 def lcg_draws_scalar(seed: int, n: int) -> np.ndarray:
@@ -127,13 +143,66 @@ def uniform_fp16(rows: int, cols: int, seed: int) -> np.ndarray:
     return fill_fp16(rows, cols, seed, -1024, 1023, 1.0 / 1024)
 
 
-def normal_fp16(rows: int, cols: int, seed: int, mean: float = 0.0, std: float = 1.0) -> np.ndarray:
-    """N(mean, std) fp16 from the LCG stream (extension of this repository): draw pairs (d0, d1)
-    give u = (d + 0.5) / 2**24 in (0, 1); z = sqrt(-2 ln u0) cos(2 pi u1) (float64), then
-    mean + std * z rounded RNE to fp16. One pair per element."""
+_h = lambda x: np.float32(float.fromhex(x))  # noqa: E731  (exact fp32 constants)
+_SQRT2, _LN2 = _h("0x1.6a09e6p+0"), _h("0x1.62e43p-1")
+_ATANH = [_h(x) for x in ("0x1.3b13b2p-4", "0x1.745d18p-4", "0x1.c71c72p-4", "0x1.24924ap-3", "0x1.99999ap-3",
+                          "0x1.555556p-2")]                      # 1/13, 1/11, ..., 1/3
+_COS = [_h(x) for x in ("-0x1.a6d1f2p-16", "0x1.e1f506p-11", "-0x1.55d3c8p-6", "0x1.03c1f0p-2", "-0x1.3bd3ccp+0")]
+_SIN = [_h(x) for x in ("-0x1.e3075p-19", "0x1.507834p-13", "-0x1.32d2ccp-8", "0x1.466bc6p-4", "-0x1.4abbcep-1",
+                        "0x1.921fb6p+0")]
+_ONE, _TWO, _HALF = np.float32(1.0), np.float32(2.0), np.float32(0.5)
+
+
+def ln_exact(u: np.ndarray) -> np.ndarray:
+    """ln u (float32, u in (0, 1], normal) as the fixed sequence of correctly rounded fp32 operations of the
+    library's generator: u = m 2^e with m in [sqrt(1/2), sqrt(2)), ln u = e ln2 + 2 atanh(t), t = (m-1)/(m+1),
+    atanh(t) = t + t^3/3 + ... + t^13/13 in Horner form."""
+    b = u.astype(np.float32).view(np.uint32)
+    e = (b >> np.uint32(23)).astype(np.int32) - 127
+    m = ((b & np.uint32(0x7FFFFF)) | np.uint32(0x3F800000)).view(np.float32)
+    big = m > _SQRT2
+    m = np.where(big, m * _HALF, m)
+    e = e + big.astype(np.int32)
+    t = (m - _ONE) / (m + _ONE)
+    t2 = t * t
+    p = np.full_like(t, _ATANH[0])
+    for c in _ATANH[1:]:
+        p = c + t2 * p
+    lnm = (t + t * (t2 * p)) * _TWO
+    return e.astype(np.float32) * _LN2 + lnm
+
+
+def cos2pi_exact(u: np.ndarray) -> np.ndarray:
+    """cos(2 pi u) (float32, u in [0, 1]): 4u = q + r, q = rint(4u), |r| <= 1/2; the quadrant q mod 4 selects
+    +-cos / +-sin of (pi/2) r, each a Taylor polynomial in r (to r^10 / r^11) of correctly rounded fp32 steps."""
+    x = u.astype(np.float32) * np.float32(4.0)
+    q = np.rint(x)
+    r = x - q
+    r2 = r * r
+    c = np.full_like(r, _COS[0])
+    for k in _COS[1:]:
+        c = k + r2 * c
+    c = _ONE + r2 * c
+    sn = np.full_like(r, _SIN[0])
+    for k in _SIN[1:]:
+        sn = k + r2 * sn
+    sn = r * sn
+    qi = q.astype(np.int32) & 3
+    return np.select([qi == 0, qi == 1, qi == 2], [c, -sn, -c], sn).astype(np.float32)
+
+
+def normal_fp16(rows: int, cols: int, seed: int, mean: float = 0.0, std: float = 1.0, row0: int = 0) -> np.ndarray:
+    """N(mean, std) fp16 from the LCG stream (an extension of this repository; the reference's LCG only yields
+    scaled integers). One draw pair (d0, d1) per element, row-major: u = (float32(d) + 0.5) * 2^-24,
+    z = sqrt(-2 ln u0) * cos(2 pi u1) with ln_exact / cos2pi_exact, value = fp16_rne(mean + std * z), every step
+    one correctly rounded float32 operation. The library's generators (sh_cuda_fill_normal_fp16 on the device,
+    sh_cuda_host_fill_normal_fp16 on the host) perform the same operations, so the bits agree. With `row0`, rows
+    row0 .. row0 + rows - 1 of that matrix (the stream jumped ahead by 2 * row0 * cols draws)."""
     n = rows * cols
-    d = lcg_draws(seed, 2 * n).astype(np.float64)
-    u0 = (d[0::2] + 0.5) / float(1 << 24)
-    u1 = (d[1::2] + 0.5) / float(1 << 24)
-    z = np.sqrt(-2.0 * np.log(u0)) * np.cos(2.0 * np.pi * u1)
-    return (mean + std * z).astype(np.float16).reshape(rows, cols)
+    d = lcg_draws(seed, 2 * n, 2 * row0 * cols)
+    k = np.float32(2.0 ** -24)
+    u0 = (d[0::2].astype(np.float32) + _HALF) * k
+    u1 = (d[1::2].astype(np.float32) + _HALF) * k
+    z = np.sqrt(np.float32(-2.0) * ln_exact(u0)) * cos2pi_exact(u1)
+    v = np.float32(mean) + np.float32(std) * z
+    return v.astype(np.float16).reshape(rows, cols)

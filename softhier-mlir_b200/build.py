@@ -23,7 +23,7 @@ LIB = PKG / "lib" / "libsh_ops_cuda.so"
 INCLUDE = ROOT / "include"
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-O2", "-I", str(INCLUDE), "-I", str(CSRC),
+FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-O2,-ffp-contract=off", "-I", str(INCLUDE), "-I", str(CSRC),
          "--expt-relaxed-constexpr"]
 
 

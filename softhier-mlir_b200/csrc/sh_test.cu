@@ -55,8 +55,92 @@ __global__ void k_fill_lcg(__half *a, uint32_t rows, uint32_t cols, uint32_t ld,
     }
 }
 
-// N(mean, std): draw pair (d0, d1) -> u = (d + 0.5) / 2^24, z = sqrt(-2 ln u0) cos(2 pi u1) (Box-Muller), one pair
-// per element in row-major order; the same definition as the host generator of the test oracle, in fp32.
+// ---- N(mean, std) with every step an IEEE-exact fp32 operation ------------------------------------------------
+// Box-Muller over one LCG draw pair (d0, d1) per element, row-major: u = (float(d) + 0.5) * 2^-24,
+// z = sqrt(-2 ln u0) * cos(2 pi u1), value = fp16_rne(mean + stdev * z). ln and cos are series of this file's own,
+// from calculus: ln u = e ln2 + 2 atanh((m - 1) / (m + 1)) with u = m 2^e, m in [sqrt(1/2), sqrt(2)), atanh to
+// t^13; cos(2 pi u) = +-cos / +-sin of (pi / 2) r with 4u = q + r, q = rint(4u), |r| <= 1/2, Taylor to r^10 / r^11.
+// Each step is one correctly rounded add / multiply / divide / sqrt in a fixed order (the _rn intrinsics on the
+// device, so nothing is contracted into an FMA; the host build disables contraction), so the host, the device and
+// the test oracle's numpy float32 restatement produce the same bits.
+#ifdef __CUDA_ARCH__
+#define RN_ADD(a, b) __fadd_rn((a), (b))
+#define RN_MUL(a, b) __fmul_rn((a), (b))
+#define RN_DIV(a, b) __fdiv_rn((a), (b))
+#define RN_SQRT(a) __fsqrt_rn(a)
+#else
+#define RN_ADD(a, b) ((a) + (b))
+#define RN_MUL(a, b) ((a) * (b))
+#define RN_DIV(a, b) ((a) / (b))
+#define RN_SQRT(a) sqrtf(a)
+#endif
+
+__host__ __device__ inline float bits_f32(uint32_t b) {
+    float f;
+    memcpy(&f, &b, 4);
+    return f;
+}
+__host__ __device__ inline uint32_t f32_bits(float f) {
+    uint32_t b;
+    memcpy(&b, &f, 4);
+    return b;
+}
+
+// ln u for normal u in (0, 1]
+__host__ __device__ inline float ln_exact(float u) {
+    const uint32_t b = f32_bits(u);
+    int e = (int)(b >> 23) - 127;
+    float m = bits_f32((b & 0x7FFFFFu) | 0x3F800000u);   // [1, 2)
+    if (m > 0x1.6a09e6p+0f) {                            // sqrt(2)
+        m = RN_MUL(m, 0.5f);
+        e += 1;
+    }
+    const float t = RN_DIV(RN_ADD(m, -1.0f), RN_ADD(m, 1.0f));
+    const float t2 = RN_MUL(t, t);
+    float p = 0x1.3b13b2p-4f;                    // 1/13
+    p = RN_ADD(0x1.745d18p-4f, RN_MUL(t2, p));   // 1/11
+    p = RN_ADD(0x1.c71c72p-4f, RN_MUL(t2, p));   // 1/9
+    p = RN_ADD(0x1.24924ap-3f, RN_MUL(t2, p));   // 1/7
+    p = RN_ADD(0x1.99999ap-3f, RN_MUL(t2, p));   // 1/5
+    p = RN_ADD(0x1.555556p-2f, RN_MUL(t2, p));   // 1/3
+    const float lnm = RN_MUL(RN_ADD(t, RN_MUL(t, RN_MUL(t2, p))), 2.0f);
+    return RN_ADD(RN_MUL((float)e, 0x1.62e43p-1f), lnm);   // ln 2
+}
+
+// cos(2 pi u) for u in [0, 1]
+__host__ __device__ inline float cos2pi_exact(float u) {
+    const float x = RN_MUL(u, 4.0f);
+    const float q = rintf(x);
+    const float r = RN_ADD(x, -q);   // exact, |r| <= 1/2
+    const float r2 = RN_MUL(r, r);
+    float c = -0x1.a6d1f2p-16f;                  // (-1)^k (pi/2)^2k / (2k)!, k = 5 .. 1, then 1
+    c = RN_ADD(0x1.e1f506p-11f, RN_MUL(r2, c));
+    c = RN_ADD(-0x1.55d3c8p-6f, RN_MUL(r2, c));
+    c = RN_ADD(0x1.03c1f0p-2f, RN_MUL(r2, c));
+    c = RN_ADD(-0x1.3bd3ccp+0f, RN_MUL(r2, c));
+    c = RN_ADD(1.0f, RN_MUL(r2, c));
+    float sn = -0x1.e3075p-19f;                  // (-1)^k (pi/2)^(2k+1) / (2k+1)!, k = 5 .. 0
+    sn = RN_ADD(0x1.507834p-13f, RN_MUL(r2, sn));
+    sn = RN_ADD(-0x1.32d2ccp-8f, RN_MUL(r2, sn));
+    sn = RN_ADD(0x1.466bc6p-4f, RN_MUL(r2, sn));
+    sn = RN_ADD(-0x1.4abbcep-1f, RN_MUL(r2, sn));
+    sn = RN_ADD(0x1.921fb6p+0f, RN_MUL(r2, sn));
+    sn = RN_MUL(r, sn);
+    switch ((int)q & 3) {
+        case 0: return c;
+        case 1: return -sn;
+        case 2: return -c;
+        default: return sn;
+    }
+}
+
+__host__ __device__ inline float normal_exact(uint32_t d0, uint32_t d1, float mean, float stdev) {
+    const float u0 = RN_MUL(RN_ADD((float)d0, 0.5f), 0x1p-24f);
+    const float u1 = RN_MUL(RN_ADD((float)d1, 0.5f), 0x1p-24f);
+    const float z = RN_MUL(RN_SQRT(RN_MUL(-2.0f, ln_exact(u0))), cos2pi_exact(u1));
+    return RN_ADD(mean, RN_MUL(stdev, z));
+}
+
 __global__ void k_fill_normal(__half *a, uint32_t rows, uint32_t cols, uint32_t ld, uint32_t seed, float mean,
                               float stdev) {
     const uint64_t total = (uint64_t)rows * cols;
@@ -68,11 +152,9 @@ __global__ void k_fill_normal(__half *a, uint32_t rows, uint32_t cols, uint32_t 
     const uint64_t end = start + kChunk < total ? start + kChunk : total;
     for (uint64_t i = start; i < end; ++i) {
         s = s * kA + kC;
-        const float u0 = ((float)(s >> 8) + 0.5f) * (1.0f / 16777216.0f);
+        const uint32_t d0 = s >> 8;
         s = s * kA + kC;
-        const float u1 = ((float)(s >> 8) + 0.5f) * (1.0f / 16777216.0f);
-        const float z = sqrtf(-2.0f * logf(u0)) * cospif(2.0f * u1);
-        a[r * ld + c] = __float2half_rn(mean + stdev * z);
+        a[r * ld + c] = __float2half_rn(normal_exact(d0, s >> 8, mean, stdev));
         if (++c == cols) {
             c = 0;
             ++r;
@@ -148,6 +230,18 @@ void sh_cuda_fill_normal_fp16(uint64_t a, uint32_t rows, uint32_t cols, uint32_t
     const uint32_t grid = (uint32_t)((threads + 255) / 256);
     k_fill_normal<<<grid, 256, 0, sh::stream()>>>((__half *)a, rows, cols, ld, seed, mean, stdev);
     sh::cuda_ok(cudaGetLastError(), "sh_cuda_fill_normal_fp16");
+}
+
+void sh_cuda_host_fill_normal_fp16(uint16_t *dst, uint32_t rows, uint32_t cols, uint32_t ld, uint32_t seed, float mean,
+                                   float stdev) {
+    if (!dst) return;
+    uint32_t s = seed ^ kSeedXor;
+    for (uint32_t r = 0; r < rows; ++r)
+        for (uint32_t c = 0; c < cols; ++c) {
+            const uint32_t d0 = host_lcg(&s);
+            const uint32_t d1 = host_lcg(&s);
+            dst[(size_t)r * ld + c] = sh_f32_to_fp16(normal_exact(d0, d1, mean, stdev));
+        }
 }
 
 void sh_cuda_fill_lcg_block(uint64_t a, uint32_t rows, uint32_t cols, uint32_t ld, uint32_t seed, int lo, int hi,

@@ -70,6 +70,44 @@ def upload_layer(rt: Runtime, p: dict) -> LayerWeights:
                         be2=up(p["be2"]))
 
 
+# ---- the benchmark's synthetic encoder --------------------------------------------------------------
+WEIGHT_SEED0, WEIGHT_SEED_STRIDE, INPUT_SEED0 = 7000, 16, 100
+
+
+def synthetic_weight_seeds(layer: int) -> dict[str, int]:
+    """LCG seeds of layer `layer`'s N(0, 0.02) matrices ([wq|wk|wv] is one 768 x 2304 matrix, filled row-major)."""
+    s = WEIGHT_SEED0 + WEIGHT_SEED_STRIDE * layer
+    return {"wqkv": s, "wo": s + 1, "w1": s + 2, "w2": s + 3}
+
+
+def synthetic_encoder(rt: Runtime, B: int, S: int, D: int, F: int, nlayers: int,
+                      input_seed: int) -> tuple[list[LayerWeights], Activations, int]:
+    """Device weights, activations and input of the synthetic encoder, generated on the GPU with the library's
+    N(mean, std) fill (sh_cuda_fill_normal_fp16, bit-identical to its host definition): per layer N(0, 0.02)
+    matrices with the seeds of synthetic_weight_seeds, zero biases, gamma 1, beta 0; the input x [B*S, D] is
+    N(0, 1) from `input_seed`. Returns (layers, activations, x address)."""
+    lib = rt.lib
+    layers = []
+    for li in range(nlayers):
+        a = rt.alloc
+        w = LayerWeights(wqkv=a(D, 3 * D), bqkv=a(1, 3 * D), wo=a(D, D), bo=a(1, D), w1=a(D, F), b1=a(1, F),
+                         w2=a(F, D), b2=a(1, D), g1=a(1, D), be1=a(1, D), g2=a(1, D), be2=a(1, D))
+        sd = synthetic_weight_seeds(li)
+        lib.sh_cuda_fill_normal_fp16(w.wqkv, D, 3 * D, 3 * D, sd["wqkv"], 0.0, 0.02)
+        lib.sh_cuda_fill_normal_fp16(w.wo, D, D, D, sd["wo"], 0.0, 0.02)
+        lib.sh_cuda_fill_normal_fp16(w.w1, D, F, F, sd["w1"], 0.0, 0.02)
+        lib.sh_cuda_fill_normal_fp16(w.w2, F, D, D, sd["w2"], 0.0, 0.02)
+        for b, n in ((w.bqkv, 3 * D), (w.bo, D), (w.b1, F), (w.b2, D), (w.be1, D), (w.be2, D)):
+            lib.sh_test_fill_const_fp16(b, 1, n, n, 0x0000)
+        for g in (w.g1, w.g2):
+            lib.sh_test_fill_const_fp16(g, 1, D, D, 0x3C00)
+        layers.append(w)
+    act = alloc_activations(rt, B, S, D, F)
+    x_in = rt.alloc(B * S, D)
+    lib.sh_cuda_fill_normal_fp16(x_in, B * S, D, D, input_seed, 0.0, 1.0)
+    return layers, act, x_in
+
+
 def alloc_activations(rt: Runtime, B: int, S: int, D: int, F: int) -> Activations:
     M = B * S
     a = rt.alloc

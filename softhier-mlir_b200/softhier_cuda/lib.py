@@ -95,6 +95,7 @@ SIGNATURES: dict[str, tuple] = {
     "sh_cuda_add_layernorm": (None, [u64, u64, u64, u64, u64, u64, u32, u32, u32, f32]),
     "sh_cuda_attention_batched": (i32, [u64, u64, u64, u64, u32, u32, u32, u32, u32, u32, u32, f32, u32]),
     "sh_cuda_fill_normal_fp16": (None, [u64, u32, u32, u32, u32, f32, f32]),
+    "sh_cuda_host_fill_normal_fp16": (None, [vp, u32, u32, u32, u32, f32, f32]),
     "sh_cuda_gemm_splitk_noalloc": (i32, [u64, u64, u64, u32, u32, u32, u32, u32, u32, u64, u64, u32, u32, u32]),
     "sh_cuda_fill_lcg_block": (None, [u64, u32, u32, u32, u32, i32, i32, f32, u64, u64, u64]),
     "sh_cuda_ipc_alloc": (vp, [sz]), "sh_cuda_ipc_free": (i32, [vp]), "sh_cuda_ipc_handle": (i32, [vp, vp]),

@@ -1,9 +1,8 @@
 """Generate the golden fixtures in this folder from the reference's own Python modules.
 
-Run where a checkout of runwangdl/softhier-mlir is available; set SOFTHIER_REF to its path (the default is where
-the build environment mounts it):
+Run where a checkout of runwangdl/softhier-mlir is available, with SOFTHIER_REF set to its path:
 
-    python tests/golden/make_golden.py
+    SOFTHIER_REF=<checkout> python tests/golden/make_golden.py
 
 It imports the reference's host-side code, never this repository's oracle, and writes:
   lcg.npz            draws of softhier_mlir.testing.lcg._lcg_stream, fill_fp16 / const / col-parity
@@ -31,7 +30,10 @@ HERE = Path(__file__).resolve().parent
 
 
 def _ref_root() -> Path:
-    return Path(os.environ.get("SOFTHIER_REF", "/root/reference"))
+    """The reference checkout (runwangdl/softhier-mlir) named by SOFTHIER_REF."""
+    if not os.environ.get("SOFTHIER_REF"):
+        raise SystemExit("set SOFTHIER_REF to a checkout of the reference (runwangdl/softhier-mlir)")
+    return Path(os.environ["SOFTHIER_REF"])
 
 
 def _q_block_rule(S: int, dh: int, H: int, cluster: int) -> int:

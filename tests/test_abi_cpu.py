@@ -81,3 +81,20 @@ def test_build_uses_sm100a_and_no_forbidden_forms():
     assert "__trap" not in src and "asm(\"trap" not in src
     build = (ROOT / "softhier-mlir_b200" / "build.py").read_text()
     assert "arch=compute_100a,code=sm_100a" in build
+
+
+def test_host_normal_generator_matches_the_oracle_bit_for_bit(lib_path):
+    """sh_cuda_host_fill_normal_fp16 (the library's N(mean, std) definition, run on the CPU) == oracle.lcg.normal_fp16
+    for every element, including a strided destination; the device kernel evaluates the same host/device function."""
+    import numpy as np
+
+    from oracle import lcg
+    from softhier_cuda import lib as L
+    lib = L.load(lib_path)
+    for rows, cols, seed, mean, std in ((64, 96, 7, 0.0, 1.0), (3, 1000, 11, 1.0, 0.02), (257, 33, 0, -0.5, 3.0)):
+        ld = cols + 5
+        buf = np.full((rows, ld), 0x7E00, np.uint16)
+        lib.sh_cuda_host_fill_normal_fp16(buf.ctypes.data, rows, cols, ld, seed, mean, std)
+        want = lcg.normal_fp16(rows, cols, seed, mean, std).view(np.uint16)
+        assert np.array_equal(buf[:, :cols], want), (rows, cols, seed)
+        assert (buf[:, cols:] == 0x7E00).all()

@@ -27,7 +27,7 @@ def test_layer_baseline_distributions_s256(gpu_lib):
     want = siglip.layer_reference_arrays(x, p, 12, scale=0.125, rounding=False)["OUT"]
     got = encoder.run_layer_once(gpu_lib, x, p, 12, 1e-6, 0.125).astype(np.float32)
     err, rel = ops.max_abs_and_rel_l2(got, want)
-    assert err <= 2e-2 * max(1.0, float(np.abs(want).max()) / 4) and rel <= 5e-3, (err, rel)
+    assert err <= 2e-2 and rel <= 5e-3, (err, rel)
 
 
 def test_batched_two_layers(gpu_lib):
@@ -47,7 +47,7 @@ def test_batched_two_layers(gpu_lib):
         sl = slice(b * S, (b + 1) * S)
         want = siglip.encoder_reference(x[sl], layers, H, scale=1.0 / np.sqrt(D // H), rounding=False)
         err, rel = ops.max_abs_and_rel_l2(got[sl], want)
-        assert rel <= 5e-3, (b, err, rel)
+        assert err <= 2e-2 and rel <= 5e-3, (b, err, rel)
 
 
 def _run_folded(rt, x, layers, B, S, H, scale):

@@ -84,3 +84,23 @@ def test_preload_elf_into_arena(gpu_lib):
         np.testing.assert_array_equal(got, seg)
     lib.sh_preload_wait(lib.sh_hbm_addr(int(g["offsets"][-1])))
     rt.check()
+
+
+def test_normal_fill_is_bit_exact_with_the_oracle(gpu_lib):
+    """sh_cuda_fill_normal_fp16 on the device == oracle.lcg.normal_fp16 for every element (strided destination,
+    a chunk boundary inside a row, a non-default mean / std), and leaves the padding columns alone."""
+    import numpy as np
+
+    from oracle import lcg
+    rt, lib = gpu_lib, gpu_lib.lib
+    rt.reset()
+    for rows, cols, seed, mean, std in ((300, 77, 5, 0.0, 1.0), (768, 2304, 7000, 0.0, 0.02), (5, 4099, 3, 1.0, 0.5)):
+        ld = cols + 13
+        a = rt.alloc(rows, ld)
+        rt.view(a, rows, ld).fill_(7.0)
+        lib.sh_cuda_fill_normal_fp16(a, rows, cols, ld, seed, mean, std)
+        got = rt.get(a, rows, ld, ld)
+        want = lcg.normal_fp16(rows, cols, seed, mean, std)
+        assert np.array_equal(got[:, :cols].view(np.uint16), want.view(np.uint16)), (rows, cols, seed)
+        assert (got[:, cols:] == 7.0).all()
+    rt.check()
