@@ -71,13 +71,30 @@ def barrier(world: int):
 
 
 def max_over_ranks(v: float, world: int) -> float:
+    """The largest `v` over all ranks (an all-reduce on the process group's device: CUDA for NCCL, CPU for gloo)."""
     if world == 1:
         return v
     import torch
     import torch.distributed as dist
-    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dev = "cuda" if dist.get_backend() == "nccl" else "cpu"
+    t = torch.tensor([v], dtype=torch.float64, device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
+
+
+def encoder_shard(world: int, rank: int) -> tuple[int, int]:
+    """(sequences on this rank, the seed of its input shard): the global batch splits evenly over the ranks; every
+    rank generates the same weights and its own input shard, so no data moves between GPUs inside a step."""
+    if GLOBAL_BATCH % world:
+        raise SystemExit(f"global batch {GLOBAL_BATCH} does not split over {world} ranks")
+    from softhier_cuda import encoder
+    return GLOBAL_BATCH // world, encoder.INPUT_SEED0 + rank
+
+
+def job_rate(ms_local: float, steps: int, world: int) -> tuple[float, float]:
+    """(ms of the slowest rank, whole-job images/s): the timed region ends when the last rank's last step ends."""
+    ms = max_over_ranks(ms_local, world)
+    return ms, GLOBAL_BATCH * steps / (ms / 1e3)
 
 
 def peaks() -> tuple[dict, str]:
@@ -221,11 +238,11 @@ class ClockSampler:
 
 
 # ---- the GPU arm -----------------------------------------------------------------------------------------------------
-def setup_encoder(rt, B: int, rank: int, nlayers: int = NLAYERS):
+def setup_encoder(rt, B: int, input_seed: int, nlayers: int = NLAYERS):
     """Device weights (identical on every rank) and activations for a shard of B sequences: the library's synthetic
-    encoder (softhier_cuda.encoder.synthetic_encoder), input seed 100 + rank."""
+    encoder (softhier_cuda.encoder.synthetic_encoder)."""
     from softhier_cuda import encoder
-    return encoder.synthetic_encoder(rt, B, S, D, F, nlayers, encoder.INPUT_SEED0 + rank)
+    return encoder.synthetic_encoder(rt, B, S, D, F, nlayers, input_seed)
 
 
 def schedule_maker(rt, act, layers, M: int, fold: bool):
@@ -249,15 +266,13 @@ def run_ours(args, rank: int, world: int, local: int) -> dict | None:
     from softhier_cuda.runtime import Runtime
 
     init_dist(world, local)
-    if GLOBAL_BATCH % world:
-        raise SystemExit(f"global batch {GLOBAL_BATCH} does not split over {world} ranks")
-    B = GLOBAL_BATCH // world
+    B, input_seed = encoder_shard(world, rank)
     M = B * S
     arena = ((17 * M * D + (M * F - M * D) + NLAYERS * (7 * D * D + 3 * D * F + 16 * F)) * 2 + 2 * M * (D // 64) * 8
              + (256 << 20))
     rt = Runtime.open(local, arena_bytes=arena)
     lib = rt.lib
-    layers, act, x_in = setup_encoder(rt, B, rank)
+    layers, act, x_in = setup_encoder(rt, B, input_seed)
     make_schedule = schedule_maker(rt, act, layers, B * S, args.ln_fold)
     rt.check()
     sched, res = make_schedule(x_in, None)
@@ -330,9 +345,8 @@ def run_ours(args, rank: int, world: int, local: int) -> dict | None:
     e1.synchronize()
     clock_info = clocks.stop()
     barrier(world)
-    ms = max_over_ranks(e0.elapsed_time(e1), world)
+    ms, value = job_rate(e0.elapsed_time(e1), args.steps, world)
     rt.check()
-    value = GLOBAL_BATCH * args.steps / (ms / 1e3)
 
     # ---- e2e: host input -> device -> encoder -> host output every step ----------------------------------------------
     # Every step copies its input batch from pinned host memory and its result back. The copies of neighbouring
@@ -680,7 +694,7 @@ def run_layer(args, local: int) -> dict:
     from softhier_cuda.runtime import Runtime
     rt = Runtime.open(local, arena_bytes=96 << 20)
     lib = rt.lib
-    layers, act, x_in = setup_encoder(rt, 1, 0, nlayers=1)
+    layers, act, x_in = setup_encoder(rt, 1, 100, nlayers=1)
     sched, _ = schedule_maker(rt, act, layers, S, args.ln_fold)(x_in, None)
     stream = torch.cuda.Stream(device=local)
     rt.activate(stream)
@@ -723,12 +737,13 @@ def run_rowops(args, local: int) -> dict:
     from softhier_cuda import lib as L
     from softhier_cuda.runtime import Runtime
     rows = 131072
-    rt = Runtime.open(local, arena_bytes=(5 << 30))
+    widths = tuple(int(c) for c in args.rowops_cols.split(","))
+    rt = Runtime.open(local, arena_bytes=6 * rows * max(widths) * 2 + (64 << 20))
     lib = rt.lib
     stream = torch.cuda.Stream(device=local)
     out = {}
     pk, src = peaks()
-    for cols in (768, 3072):
+    for cols in widths:
         rt.reset()
         nbuf = 2
         xs = [rt.alloc(rows, cols) for _ in range(nbuf)]
@@ -768,7 +783,7 @@ def run_rowops(args, local: int) -> dict:
     return {"metric": "row-op GB/s (HBM-resident)", "value": round(min(v["gbs"] for v in out.values()), 1),
             "unit": "GB/s (slowest op)", "n_gpus": 1, "higher_is_better": True, "dtype": "f16", "ops": out,
             "min_frac_hbm": worst, "peak": f"{src} copy {pk['hbm_gbs']} GB/s",
-            "small": _rowops_small(torch, rt, stream),
+            "small": _rowops_small(torch, rt, stream) if not args.no_small else None,
             "config": {"workload": "BASELINE config 2 ops at 131072 x {768, 3072}; 'small': the 256-row shapes",
                        "l2": "2 rotating buffer sets of 201 / 805 MB per operand (> 2 x L2)"}}
 
@@ -930,6 +945,8 @@ def main():
     ap.add_argument("--gemm", default="131072,3072,768", help="M,N,K of --workload gemm")
     ap.add_argument("--epi", default="bias,gelu", help="fused epilogue of --workload gemm: bias,gelu,residual")
     ap.add_argument("--summa-n", type=int, default=16384)
+    ap.add_argument("--rowops-cols", default="768,3072", help="row widths of --workload rowops (131072 rows each)")
+    ap.add_argument("--no-small", action="store_true", help="--workload rowops: skip the 256-row graph timings")
     ap.add_argument("--vs-cublas", action="store_true", help="--workload gemm: also time torch.matmul on the shape")
     args = ap.parse_args()
     rank, world, local = dist_env()

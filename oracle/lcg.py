@@ -83,10 +83,11 @@ def lcg_draws_scalar(seed: int, n: int) -> np.ndarray:
     return out
 
 
-def fill_fp16(rows: int, cols: int, seed: int, lo: int, hi: int, scale: float = 1.0) -> np.ndarray:
-    """sh_test_fill_fp16 (sh_test.inc.c:4-13): integers in [lo, hi] times scale, fp16 RNE, row-major."""
+def fill_fp16(rows: int, cols: int, seed: int, lo: int, hi: int, scale: float = 1.0, row0: int = 0) -> np.ndarray:
+    """sh_test_fill_fp16 (sh_test.inc.c:4-13): integers in [lo, hi] times scale, fp16 RNE, row-major. With `row0`,
+    rows row0 .. row0 + rows - 1 of that matrix."""
     span = int(hi) - int(lo) + 1
-    ints = (lcg_draws(seed, rows * cols) % np.uint32(span)).astype(np.int64) + int(lo)
+    ints = (lcg_draws(seed, rows * cols, row0 * cols) % np.uint32(span)).astype(np.int64) + int(lo)
     return (ints.astype(np.float32) * np.float32(scale)).astype(np.float16).reshape(rows, cols)
 
 
@@ -138,9 +139,9 @@ def compare_samples(samples, ref: np.ndarray, atol: float, rtol: float) -> tuple
 
 # ---- BASELINE input distributions -------------------------------------------------------
 
-def uniform_fp16(rows: int, cols: int, seed: int) -> np.ndarray:
+def uniform_fp16(rows: int, cols: int, seed: int, row0: int = 0) -> np.ndarray:
     """uniform [-1, 1) as k/1024 (exact reference semantics: fill_fp16(.., -1024, 1023, 1/1024))."""
-    return fill_fp16(rows, cols, seed, -1024, 1023, 1.0 / 1024)
+    return fill_fp16(rows, cols, seed, -1024, 1023, 1.0 / 1024, row0)
 
 
 _h = lambda x: np.float32(float.fromhex(x))  # noqa: E731  (exact fp32 constants)

@@ -126,3 +126,31 @@ def test_emitted_program_compiles_and_links(tmp_path, passes):
     r = subprocess.run(["gcc", "-O1", "-Wall", "-Wno-unused-variable", "-Werror", "-I", str(ROOT / "include"), str(src), "-L", str(lib),
                         "-lsh_ops_cuda", "-o", str(tmp_path / "main")], capture_output=True, text=True)
     assert r.returncode == 0, r.stderr
+
+
+def test_looped_encoder_lowering(tmp_path):
+    """scf.for lowering of a compact multi-layer module (tests/looped_module.py): the layer loop becomes a C for loop,
+    every indexed parameter buffer `offset + i * stride`, the nested GELU loop indexed column views of FC1's output,
+    and the indexed dump appends the layer number (the rules of the reference's loop_translate.mlir:26-37); the
+    program compiles and links against the library."""
+    import looped_module as LM
+    S, D, F, H, NL = 64, 128, 256, 2, 3
+    act, poff, stride, base = LM.layout(S, D, F)
+    c = E.emit_c(LM.looped_encoder(S, D, F, H, NL))
+    body = c.split("static void looped_encoder(void) {")[1]
+    assert "for (uint32_t i1 = 0; i1 < 3; i1 += 1) {" in body
+    assert f"sh_hbm_addr((uint64_t){base + poff['w1']} + (uint64_t)(i1) * {stride}u);" in body
+    assert "for (uint32_t i2 = 0; i2 < 4; i2 += 1) {" in body
+    # gelu over column block i2 of f1 (hb10) into g (hb11): 64 columns = 128 bytes per block
+    assert "sh_gelu((hb11 + (uint64_t)(i2) * 128u), (hb10 + (uint64_t)(i2) * 128u), 64, 64, 256, SH_ALL);" in body
+    assert 'sh_test_dump_samples_idx(hb1, 64, 128, 128, 7, 32, "L", (uint32_t)((i1 + 1)));' in body
+    assert body.count("sh_gemm(") == 6 and "unsupported" not in c
+    lib = ROOT / "softhier-mlir_b200" / "lib"
+    if shutil.which("gcc") is None or not (lib / "libsh_ops_cuda.so").exists():
+        pytest.skip("no C compiler or library")
+    src = tmp_path / "main.c"
+    src.write_text(c)
+    r = subprocess.run(["gcc", "-O1", "-Wall", "-Wno-unused-variable", "-Werror", "-I", str(ROOT / "include"),
+                        str(src), "-L", str(lib), "-lsh_ops_cuda", "-o", str(tmp_path / "main")],
+                       capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr

@@ -118,3 +118,40 @@ def test_emitted_c_program_runs(tmp_path):
     assert "KAT1024_CHECK ok=1048576/1048576 KAT1024_PASS" in r.stdout
     assert "[Performance Counter]: Execution period is" in r.stdout
     assert "[sh_" not in r.stdout
+
+
+@pytest.mark.parametrize("S,D,F,H,NL", [(64, 128, 256, 2, 3), (256, 768, 3072, 12, 2)])
+def test_looped_encoder_module_on_gpu(gpu_lib, capfd, S, D, F, H, NL):
+    """A looped multi-layer module (scf.for over layers with indexed parameter buffers, a nested loop over indexed
+    GELU column views; tests/looped_module.py) run through emit_cuda.Program: the residual stream after every layer
+    (indexed dumps L1..Ln) and the final output match the stacked oracle layers with the reference's LCG
+    parameters (frontend seeds 100 * layer) within the reference's 0.05 / 0.05 (run.py:360-365)."""
+    import looped_module as LM
+    rt = gpu_lib
+    rt.reset()
+    text = LM.looped_encoder(S, D, F, H, NL)
+    prog = E.Program(text, rt)
+    act, poff, stride, base = LM.layout(S, D, F)
+    x, _ = siglip.lcg_layer_inputs(S, D, F, 0)
+    params = [siglip.lcg_layer_inputs(S, D, F, li)[1] for li in range(NL)]
+    rt.put(rt.lib.sh_hbm_addr(act["x"]), x)
+    for li, p in enumerate(params):
+        for name in LM.PARAMS:
+            rt.put(rt.lib.sh_hbm_addr(base + li * stride + poff[name]), p[name])
+    capfd.readouterr()
+    assert prog.run() == 0
+    rt.check()
+    out = capfd.readouterr().out
+    got = lcg.parse_samples(out)
+    cur = x
+    scale = 1.0 / np.sqrt(D // H)
+    for li in range(NL):
+        cur = siglip.layer_reference_arrays(cur, params[li], H, scale=scale)["OUT"]
+        tag = f"L{li + 1}"
+        assert len(got[tag]) == 32, tag
+        bad, err = lcg.compare_samples(got[tag], cur, 0.05, 0.05)
+        assert bad == 0, (tag, err)
+        assert f"[mark] layer{li + 1} " in out
+    final = prog.tensor("x").astype(np.float32)
+    err = np.abs(final - cur)
+    assert np.all(err <= 0.05 + 0.05 * np.abs(cur)), float(err.max())

@@ -53,6 +53,58 @@ def test_summa_single_gpu_panels(gpu_lib, kb):
         su.close()
 
 
+@pytest.mark.parametrize("kb", [16384, 4096])
+def test_summa_config4_size_sampled(gpu_lib, capfd, kb):
+    """BASELINE config 4 at full size on one GPU (16384^3, uniform [-1, 1) from the LCG): the block fill is
+    bit-exact on sampled rows of A, and 64 sampled outputs match float64 dot products of the stored operands within
+    half an fp16 ulp of the result plus 2e-3; the reference's own sampled check (sh_test_check_gemm,
+    runtime/sh_test.inc.c:32-51) passes on 256 more positions. kb = 4096 carries the sum over four panels in fp32."""
+    lib = gpu_lib.lib
+    n = 16384
+    lay = SU.Layout(n, n, n, 1, 1, kb)
+    su = SU.SummaGPU(lib, lay, 0, lambda x: [x], lambda: None, (torch.cuda.Stream(), torch.cuda.Stream()))
+    try:
+        su.fill_inputs(5, 6)
+        assert su.step(torch) == 0
+        torch.cuda.synchronize()
+        gpu_lib.check()
+
+        def dev(addr, rows, cols, ld):
+            t = torch.empty((rows, cols), dtype=torch.float16, device="cuda")
+            lib.sh_cuda_copy2d(t.data_ptr(), cols * 2, addr, ld * 2, cols * 2, rows, None)
+            torch.cuda.synchronize()
+            return t.cpu().numpy()
+
+        rng = np.random.default_rng(4)
+        rows = rng.integers(0, n, 8)
+        cols = rng.integers(0, n, 8)
+        for r in rows[:3]:
+            want = lcg.uniform_fp16(1, n, 5, row0=int(r))
+            assert np.array_equal(dev(su.a_loc + 2 * int(r) * n, 1, n, n).view(np.uint16), want.view(np.uint16))
+        a_rows = {int(r): dev(su.a_loc + 2 * int(r) * n, 1, n, n)[0].astype(np.float64) for r in rows}
+        b_cols = {int(c): dev(su.b_loc + 2 * int(c), n, 1, n)[:, 0].astype(np.float64) for c in cols}
+        worst = 0.0
+        for r in a_rows:
+            zrow = dev(su.c + 2 * r * n, 1, n, n)[0].astype(np.float64)
+            for c in b_cols:
+                want = float(a_rows[r] @ b_cols[c])
+                ulp = 2.0 ** (np.floor(np.log2(max(abs(want), 2.0 ** -14))) - 10)
+                err = abs(zrow[c] - want)
+                worst = max(worst, err / (0.5 * ulp + 2e-3))
+                assert err <= 0.5 * ulp + 2e-3, (r, c, zrow[c], want)
+        capfd.readouterr()
+        lib.sh_cuda_set_stream(None)
+        bad = lib.sh_test_check_gemm(su.a_loc, su.b_loc, su.c, n, n, n, n, n, n, 256, 0.25, 0.0, b"[summa16384]")
+        gpu_lib.activate()
+        out = capfd.readouterr().out
+        assert bad == 0 and "[summa16384] samples=256 bad=0" in out, out
+        print(f"config 4 sampled: worst error / bound {worst:.3f}")
+    finally:
+        torch.cuda.synchronize()
+        su.close()
+        gpu_lib.activate()
+
+
 # panel width 128: every panel one piece per operand; 512 = n / 2: on 2x4 each A panel spans two owners' blocks;
 # 1024 = n (the default): one panel per step, pulled during the previous step's GEMM
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
