@@ -245,7 +245,7 @@ def setup_encoder(rt, B: int, input_seed: int, nlayers: int = NLAYERS):
     return encoder.synthetic_encoder(rt, B, S, D, F, nlayers, input_seed)
 
 
-def schedule_maker(rt, act, layers, M: int, fold: bool):
+def schedule_maker(rt, act, layers, M: int, fold: str):
     """(x_in, x_out) -> (calls of one forward pass, result address). By default the 7-launch layer (separate
     LayerNorm kernels); with --ln-fold both LayerNorms of every layer are folded into the GEMMs that consume them
     (sh_cuda_gemm_ln: 1 + 5 launches per layer after a one-time weight transform). The folded form measured ~1 %
@@ -253,8 +253,12 @@ def schedule_maker(rt, act, layers, M: int, fold: bool):
     cost."""
     from softhier_cuda import encoder
     lib = rt.lib
-    if not fold:
+    if fold == "none":
         return lambda xi, xo: encoder.encoder_schedule(lib, act, layers, H, EPS, SCALE, xi, xo)
+    if fold == "ln1":
+        folded1 = [encoder.fold_layer_norm1(rt, w, D) for w in layers]
+        stats_x = encoder.alloc_row_stats(rt, M, D)[0]
+        return lambda xi, xo: encoder.encoder_schedule_ln1_folded(lib, act, folded1, stats_x, H, EPS, SCALE, xi, xo)
     folded = [encoder.fold_layer_norms(rt, w, D, F) for w in layers]
     stats = encoder.alloc_row_stats(rt, M, D)
     return lambda xi, xo: encoder.encoder_schedule_folded(lib, act, folded, stats, H, EPS, SCALE, xi, xo)
@@ -376,7 +380,7 @@ def run_ours(args, rank: int, world: int, local: int) -> dict | None:
         else:
             slot_step.append((None, enqueue_s))
     h2d, d2h = torch.cuda.Stream(device=local), torch.cuda.Stream(device=local)
-    e2e_steps = max(3, args.steps // 2)
+    e2e_steps = args.steps                   # the same step count as the device-resident leg
     in_ready = [torch.cuda.Event(), torch.cuda.Event()]
     done = [torch.cuda.Event(), torch.cuda.Event()]
     out_read = [torch.cuda.Event(), torch.cuda.Event()]
@@ -406,15 +410,29 @@ def run_ours(args, rank: int, world: int, local: int) -> dict | None:
 
     e2e_run(2)                                   # warm the copy paths
     stream.synchronize()
-    barrier(world)
-    torch.cuda.synchronize()
-    e0.record(stream)
-    e2e_run(e2e_steps)
-    e1.record(stream)
-    e1.synchronize()
-    barrier(world)
-    e2e_ms = max_over_ranks(e0.elapsed_time(e1), world)
+
+    def timed(fn) -> float:
+        """ms of one timed region of K steps (barrier + synchronize on both sides, max over ranks)"""
+        barrier(world)
+        torch.cuda.synchronize()
+        e0.record(stream)
+        fn()
+        e1.record(stream)
+        e1.synchronize()
+        barrier(world)
+        return max_over_ranks(e0.elapsed_time(e1), world)
+
+    def steps_resident():
+        for _ in range(args.steps):
+            step()
+
+    e2e_ms = timed(lambda: e2e_run(e2e_steps))
     e2e_value = GLOBAL_BATCH * e2e_steps / (e2e_ms / 1e3)
+    # two more regions of each leg, alternating, so that both legs are compared at the same clocks
+    rep_value, rep_e2e = [ms], [e2e_ms]
+    for _ in range(2):
+        rep_value.append(timed(steps_resident))
+        rep_e2e.append(timed(lambda: e2e_run(e2e_steps)))
     rt.check()
     step()                                       # the device-resident step on the same input batch ...
     stream.synchronize()
@@ -460,6 +478,12 @@ def run_ours(args, rank: int, world: int, local: int) -> dict | None:
                    "l2": "inputs larger than L2 (201 MB per activation tensor at B=512), no flush"},
         "e2e": {"value": round(e2e_value, 1), "unit": "images/s", "h2d_bytes_per_step": M * D * 2,
                 "d2h_bytes_per_step": M * D * 2, "steps": e2e_steps},
+        "repeats": {"what": "value / e2e legs timed three times each (alternating, K steps per region); value and "
+                            "e2e above are the first region of each",
+                    "value_images_per_s": [round(GLOBAL_BATCH * args.steps / (t / 1e3), 1) for t in rep_value],
+                    "e2e_images_per_s": [round(GLOBAL_BATCH * e2e_steps / (t / 1e3), 1) for t in rep_e2e],
+                    "median_value": round(GLOBAL_BATCH * args.steps / (statistics.median(rep_value) / 1e3), 1),
+                    "median_e2e": round(GLOBAL_BATCH * e2e_steps / (statistics.median(rep_e2e) / 1e3), 1)},
         "gpu_launches": args.steps * len(sched),
         "roofline": roofline,
         "kernels": kernels,
@@ -888,6 +912,22 @@ def run_summa(args, rank: int, world: int, local: int) -> dict | None:
     barrier(world)
     ms = max_over_ranks(e0.elapsed_time(e1) / steps, world)
     rt.check()
+    # one-shot C = A B: a call whose panel pull was not started by an earlier step (the pull and the GEMM in series),
+    # after one un-timed step that consumes the timed loop's prefetch
+    assert su.step(torch, prefetch_next=False) == 0
+    torch.cuda.synchronize()
+    one_shot = []
+    for _ in range(3):
+        barrier(world)
+        torch.cuda.synchronize()
+        e0.record(compute)
+        assert su.step(torch, prefetch_next=False) == 0
+        e1.record(compute)
+        e1.synchronize()
+        one_shot.append(e0.elapsed_time(e1))
+    barrier(world)
+    one_shot_ms = max_over_ranks(statistics.median(one_shot), world)
+    rt.check()
     su.close()
     flop = 2.0 * n ** 3
     pk, src = peaks()
@@ -906,6 +946,9 @@ def run_summa(args, rank: int, world: int, local: int) -> dict | None:
             "scaling": "strong", "dtype": "f16", "frac_of_peak_per_gpu": round(tf / world / pk["bf16_tflops_sustained"], 3),
             "peak": f"{src} bf16 sustained {pk['bf16_tflops_sustained']} TFLOP/s per GPU",
             "peer_bytes_per_step_rank0": peer_bytes, "clocks": clock_info,
+            "one_shot": {"ms": round(one_shot_ms, 3), "tflops": round(flop / one_shot_ms / 1e9, 1),
+                         "what": "one C = A B whose panel pulls start with it (no overlap with an earlier step), "
+                                 "median of 3, max over ranks"},
             "config": {"workload": "BASELINE config 4: distributed SUMMA", "n": n, "grid": f"{pr}x{pc}", "panel": kb,
                        "transport": "CUDA IPC + copy engines (cudaMemcpy2DAsync) over NVLink"}}
 
@@ -935,7 +978,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-graph", action="store_true")
-    ap.add_argument("--ln-fold", action="store_true", help="fold both LayerNorms of each layer into its GEMMs")
+    ap.add_argument("--ln-fold", choices=["none", "ln1", "both"], default="none",
+                    help="LayerNorms folded into the GEMMs that consume them: none, LN1 into QKV, or both")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-images", type=int, default=2)
     ap.add_argument("--debug", action="store_true")

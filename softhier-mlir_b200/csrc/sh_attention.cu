@@ -506,19 +506,31 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&s_free[t]);
                 const int32_t valid = (int32_t)a.S - (int32_t)(j * kTcKeys);
-                if (valid < kTcKeys) {
+                if (valid < kTcKeys) {   // masked keys: s * sl2 = -inf whatever the sign of the scale
+                    const float ninf = a.sl2 >= 0.f ? -INFINITY : INFINITY;
 #pragma unroll
                     for (int i = 0; i < kTcKeys; ++i)
-                        if (i >= valid) sc[i] = -INFINITY;
+                        if (i >= valid) sc[i] = ninf;
                 }
-                // row max: eight independent chains, then a tree (a single chain would serialise 127 dependent ops)
+                // row max of s * sl2: eight independent chains, then a tree (a single chain would serialise 127
+                // dependent ops); with a negative scale the largest s * sl2 comes from the smallest s
                 float mx[8];
+                float mb;
+                if (a.sl2 >= 0.f) {
 #pragma unroll
-                for (int i = 0; i < 8; ++i) mx[i] = sc[i];
+                    for (int i = 0; i < 8; ++i) mx[i] = sc[i];
 #pragma unroll
-                for (int i = 8; i < kTcKeys; ++i) mx[i & 7] = fmaxf(mx[i & 7], sc[i]);
-                float mb = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
-                                 fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+                    for (int i = 8; i < kTcKeys; ++i) mx[i & 7] = fmaxf(mx[i & 7], sc[i]);
+                    mb = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                               fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) mx[i] = sc[i];
+#pragma unroll
+                    for (int i = 8; i < kTcKeys; ++i) mx[i & 7] = fminf(mx[i & 7], sc[i]);
+                    mb = fminf(fminf(fminf(mx[0], mx[1]), fminf(mx[2], mx[3])),
+                               fminf(fminf(mx[4], mx[5]), fminf(mx[6], mx[7])));
+                }
                 mb *= a.sl2;
                 // P V of the previous block is done: P's buffer and O may be touched
                 if (j > 0 && !mbar_wait(&o_full[t], (g - 1u) & 1u, abort, a.err)) {

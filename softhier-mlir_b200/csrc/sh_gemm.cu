@@ -270,9 +270,12 @@ __device__ __forceinline__ void epi_math_guarded(const GemmArgs &a, uint32_t row
 // One 32-column chunk of the tile per warp (thread = row): the fused epilogue, then either the warp's 32 x 32 tile
 // is staged in its shared-memory buffer (64-byte swizzle: 16-byte unit u of row r at u ^ ((r >> 1) & 3)) and written
 // by one TMA store, or every thread stores its row directly (fp32 outputs, unaligned operands).
+// `slot` non-null: stage in that buffer (it held this chunk's residual tile, already read; no earlier store is
+// pending on it) instead of the warp's two rotating buffers.
 __device__ __forceinline__ void epi_chunk(const GemmArgs &a, const CUtensorMap *mz, uint8_t *stg, uint32_t &nst,
                                           uint32_t row, uint32_t row_base, uint32_t col, float (&v)[32],
-                                          const uint4 (&res)[4], uint32_t lane, float2 ln, float2 &st) {
+                                          const uint4 (&res)[4], uint32_t lane, float2 ln, float2 &st,
+                                          uint8_t *slot = nullptr) {
     const bool inb = a.vec && row < a.M && col + 32 <= a.N;
     if (a.tma_store) {
         if (inb)
@@ -295,9 +298,11 @@ __device__ __forceinline__ void epi_chunk(const GemmArgs &a, const CUtensorMap *
                 st = make_float2(0.f, 0.f);
             }
         }
-        uint8_t *buf = stg + (nst & 1u) * 2048;
-        if (lane == 0) bulk_wait_read1();     // the store issued from this buffer two chunks ago has read it
-        __syncwarp();
+        uint8_t *buf = slot ? slot : stg + (nst & 1u) * 2048;
+        if (!slot) {
+            if (lane == 0) bulk_wait_read1();     // the store issued from this buffer two chunks ago has read it
+            __syncwarp();
+        }
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
             uint4 out;
@@ -602,16 +607,20 @@ constexpr int kPairStages = 6;
 // BN = 512: 256 x 512 pair tiles from two N = 256 MMAs per k-step into one accumulator (all 512 tensor-memory
 // columns): 25 % fewer operand bytes per MAC than 256 x 256, but the epilogue no longer overlaps the next tile's
 // main loop, so the planner uses it for long K loops only.
-template <int BN>
+// RES (BN = 256): the residual of an epilogue chunk arrives by TMA as a 32 x 32 tile in the slot its output then
+// leaves from; four slots per epilogue warp (a whole 128-column half tile, loaded one tile ahead) take the shared
+// memory of one load stage.
+template <int BN, bool RES = false>
 struct PairCfg {
-    static constexpr int kStages = BN == 512 ? 4 : kPairStages;
+    static constexpr int kStages = BN == 512 ? 4 : (RES ? kPairStages - 1 : kPairStages);
     static constexpr uint32_t kAcc = BN == 512 ? 1 : 2;          // accumulator buffers
     static constexpr uint32_t kMmaN = BN < 256 ? BN : 256;       // N of one MMA; BN / kMmaN of them per k-step
     static constexpr uint32_t kABytes = 128 * BK * 2;          // this CTA's 128 rows
     static constexpr uint32_t kBBytes = (BN / 2) * BK * 2;     // this CTA's half of every MMA's columns
     static constexpr uint32_t kStageBytes = kABytes + kBBytes;
     static constexpr uint32_t kTmemCols = kAcc * BN;
-    static constexpr uint32_t kSmem = kStages * kStageBytes + kEpiStageBytes + 1024 + 256;
+    static constexpr uint32_t kEpiBytes = RES ? 2 * kEpiStageBytes : kEpiStageBytes;   // per warp 4 or 2 slots of 2 KB
+    static constexpr uint32_t kSmem = kStages * kStageBytes + kEpiBytes + 1024 + (RES ? 512 : 256);
 };
 
 // Work unit u of the 2-CTA kernel: whole tile u below a.full_units; past it, one kMmaN-wide column slice (h0) of
@@ -632,23 +641,24 @@ __device__ __forceinline__ void pair_unit(const GemmArgs &a, uint32_t u, uint32_
     }
 }
 
-template <int BN>
+template <int BN, bool RES = false>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     k_gemm_tc2(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w,
-               const __grid_constant__ CUtensorMap map_z, GemmArgs a) {
-    using C = PairCfg<BN>;
+               const __grid_constant__ CUtensorMap map_z, const __grid_constant__ CUtensorMap map_r, GemmArgs a) {
+    using C = PairCfg<BN, RES>;
     constexpr int S = C::kStages;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
     uint8_t *smem = smem_raw + pad;
     uint8_t *epi_stage = smem + S * C::kStageBytes;
-    uint64_t *full = reinterpret_cast<uint64_t *>(epi_stage + kEpiStageBytes);
+    uint64_t *full = reinterpret_cast<uint64_t *>(epi_stage + C::kEpiBytes);
     uint64_t *empty = full + S;
     uint64_t *tfull = empty + S;
     uint64_t *tempty = tfull + 2;
     uint64_t *mdone = tempty + 2;
     uint64_t *epi_done = mdone + 1;   // [2] this CTA's 8 epilogue warps have drained accumulator buffer i
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(epi_done + 2);
+    uint64_t *res_full = epi_done + 2;   // RES: [8 warps x 4 slots] a residual tile has landed
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(res_full + (RES ? 32 : 0));
     volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -665,6 +675,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
             mbar_init(&tempty[i], 2);        // leader: warp 10 of both CTAs
             mbar_init(&epi_done[i], kEpiWarps);
         }
+        if (RES)
+            for (int i = 0; i < 32; ++i) mbar_init(&res_full[i], 1);
         mbar_init(mdone, 1);
         *abort = 0;
         fence_mbar_init();
@@ -791,10 +803,30 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
         const uint32_t half = (warp - 2u) >> 2;
         const uint32_t row_in_tile = rank * 128 + quarter * 32 + lane;
         const bool want_res = (a.flags & SH_EPI_RESIDUAL) != 0;
-        uint8_t *stg = epi_stage + (warp - 2u) * 4096u;
+        const uint32_t ew = warp - 2u;
+        uint8_t *stg = epi_stage + ew * (RES ? 8192u : 4096u);
         uint32_t nst = 0;
         if (a.tma_store && lane == 0) prefetch_tmap(&map_z);
         uint32_t acc = 0, acc_phase = 0;
+        // RES: the residual tiles of this warp's 32 rows x 128 columns of a unit, one TMA load per 32-column chunk
+        // into slot c, issued one unit ahead (after the previous unit's stores have read the slots)
+        uint32_t res_phase = 0, res_armed = 0;
+        auto load_res = [&](uint32_t u) {
+            uint32_t tile, h0, nh, tm, tn;
+            pair_unit<BN>(a, u, tile, h0, nh);
+            tile_coords(tile, a.num_tiles / a.tiles_n, a.tiles_n, a.group_m, tm, tn);
+            const int32_t y = (int32_t)(tm * 256 + rank * 128 + quarter * 32);
+#pragma unroll
+            for (uint32_t c = 0; c < 4; ++c) {
+                mbar_arrive_expect_tx(&res_full[ew * 4 + c], 2048);
+                tma_load_2d(stg + c * 2048, &map_r, &res_full[ew * 4 + c], (int32_t)(tn * BN + half * 128 + c * 32), y);
+            }
+        };
+        if (RES && lane == 0 && pair < total_units) {
+            prefetch_tmap(&map_r);
+            load_res(pair);
+            res_armed = 1;
+        }
         for (uint32_t u = pair; u < total_units; u += npairs) {
             uint32_t tile, h0, nh, tm, tn;
             pair_unit<BN>(a, u, tile, h0, nh);
@@ -804,39 +836,62 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
             const uint32_t row_base = tm * 256 + rank * 128 + quarter * 32;
             const uint32_t col0 = tn * BN + h0 * C::kMmaN + half * HB;
             uint4 res[4] = {};
-            const bool res_vec = want_res && a.vec && row < a.M;
+            const bool res_vec = !RES && want_res && a.vec && row < a.M;
             if (res_vec && col0 + 32 <= a.N) load32(a.resid + (size_t)row * a.ldr + col0, res);
             const float2 ln = ln_row(a, row);
             float2 st = make_float2(0.f, 0.f);
             if (!mbar_wait(&tfull[acc], acc_phase, abort, a.err)) break;
             tc_fence_after();
             const uint32_t taddr = tmem_base + ((quarter * 32u) << 16) + acc * BN + h0 * C::kMmaN + half * HB;
+            bool res_ok = true;
 #pragma unroll 1
             for (uint32_t c = 0; c < HB / 32; ++c) {
                 uint32_t r[32];
                 tmem_ld_32x32b_x32(taddr + c * 32, r);
-                tmem_ld_wait();
                 const uint32_t col = col0 + c * 32;
                 uint4 nres[4] = {};
                 if (res_vec && c + 1 < HB / 32 && col + 64 <= a.N)
                     load32(a.resid + (size_t)row * a.ldr + col + 32, nres);
+                uint8_t *slot = nullptr;
+                if (RES) {   // this chunk's residual tile, 64-byte swizzled like the output staging
+                    slot = stg + c * 2048;
+                    if (!mbar_wait(&res_full[ew * 4 + c], res_phase, abort, a.err)) res_ok = false;
+#pragma unroll
+                    for (int q = 0; q < 4; ++q)
+                        res[q] = *reinterpret_cast<const uint4 *>(slot + lane * 64 + ((q ^ ((lane >> 1) & 3u)) << 4));
+                }
+                tmem_ld_wait();
                 float v[32];
 #pragma unroll
                 for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
                 if (!a.tma_store || (row_base < a.M && col < a.N))
-                    epi_chunk(a, &map_z, stg, nst, row, row_base, col, v, res, lane, ln, st);
+                    epi_chunk(a, &map_z, stg, nst, row, row_base, col, v, res, lane, ln, st, slot);
+                if (!RES) {
 #pragma unroll
-                for (int i = 0; i < 4; ++i) res[i] = nres[i];
+                    for (int i = 0; i < 4; ++i) res[i] = nres[i];
+                }
             }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&epi_done[acc]);
+            if (RES) {
+                if (!res_ok) break;   // (the loads of this unit stay armed: drained below)
+                res_phase ^= 1u;
+                res_armed = 0;
+                if (lane == 0 && u + npairs < total_units) {
+                    bulk_wait_read0();   // this unit's stores have read the slots
+                    load_res(u + npairs);
+                    res_armed = 1;
+                }
+            }
             if (++acc == C::kAcc) {
                 acc = 0;
                 acc_phase ^= 1u;
             }
         }
         if (lane == 0 && nst) bulk_wait_all();
+        if (RES && lane == 0 && res_armed)   // loads issued for a unit this warp did not reach (an abort)
+            for (uint32_t c = 0; c < 4; ++c) drain_wait(&res_full[ew * 4 + c], res_phase);
     }
 
     __syncwarp();
@@ -1000,14 +1055,14 @@ PairUnits pair_units(uint32_t num_tiles, uint32_t bn, uint32_t sm_pairs) {
     return r;
 }
 
-template <int BN>
-int launch_pair(const Plan &p, const CUtensorMap &mx, const CUtensorMap &mw, const CUtensorMap &mz, GemmArgs a,
-                cudaStream_t st) {
+template <int BN, bool RES = false>
+int launch_pair(const Plan &p, const CUtensorMap &mx, const CUtensorMap &mw, const CUtensorMap &mz,
+                const CUtensorMap &mr, GemmArgs a, cudaStream_t st) {
     static bool done[sh::kMaxDevices] = {};
     const int d = sh::current_device() % sh::kMaxDevices;
     if (!done[d]) {
-        if (!sh::cuda_ok(cudaFuncSetAttribute(k_gemm_tc2<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                              (int)PairCfg<BN>::kSmem),
+        if (!sh::cuda_ok(cudaFuncSetAttribute(k_gemm_tc2<BN, RES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              (int)PairCfg<BN, RES>::kSmem),
                          "cudaFuncSetAttribute(gemm pair)"))
             return -1;
         done[d] = true;
@@ -1019,8 +1074,8 @@ int launch_pair(const Plan &p, const CUtensorMap &mx, const CUtensorMap &mw, con
     a.full_units = pu.full;
     a.num_units = pu.units;
     const uint32_t pairs = min(a.num_units, sm_pairs);
-    return sh::cuda_ok(sh::launch_pdl(k_gemm_tc2<BN>, dim3(2 * pairs), dim3(kPairThreads), PairCfg<BN>::kSmem, st, mx,
-                                  mw, mz, a),
+    return sh::cuda_ok(sh::launch_pdl(k_gemm_tc2<BN, RES>, dim3(2 * pairs), dim3(kPairThreads),
+                                      PairCfg<BN, RES>::kSmem, st, mx, mw, mz, mr, a),
                        "sh_gemm launch (pair)")
                ? 0
                : -1;
@@ -1143,7 +1198,20 @@ int gemm_run(uint64_t x, uint64_t w, uint64_t z, uint32_t M, uint32_t N, uint32_
         return -1;
     }
     if (!a.tma_store) mz = mx;   // not read by the kernel
-    if (p.pair) return p.pair_bn == 512 ? launch_pair<512>(p, mx, mw, mz, a, st) : launch_pair<256>(p, mx, mw, mz, a, st);
+    if (p.pair) {
+        // 256 x 256 tiles with an fp16 residual and TMA-stored outputs: the residual tiles come in by TMA as well
+        // (one coalesced 2 KB box per 32 x 32 chunk instead of one 16-byte load per row and thread); SH_GEMM_RES_TMA=0
+        // reads them per thread instead
+        static const bool res_tma_env = [] {
+            const char *e = getenv("SH_GEMM_RES_TMA");
+            return !(e && atoi(e) == 0);
+        }();
+        CUtensorMap mr;
+        if (p.pair_bn == 256 && res_tma_env && a.tma_store && (a.flags & SH_EPI_RESIDUAL) &&
+            make_map_2d_sw(&mr, (const void *)resid, M, N, ldr, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B))
+            return launch_pair<256, true>(p, mx, mw, mz, mr, a, st);
+        return p.pair_bn == 512 ? launch_pair<512>(p, mx, mw, mz, mx, a, st) : launch_pair<256>(p, mx, mw, mz, mx, a, st);
+    }
     switch (p.bn) {
         case 256: return launch_tc<256>(p, mx, mw, mz, a, st);
         case 128: return launch_tc<128>(p, mx, mw, mz, a, st);

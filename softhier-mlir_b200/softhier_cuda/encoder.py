@@ -181,6 +181,83 @@ def fold_layer_norms(rt: Runtime, w: LayerWeights, D: int, F: int) -> FoldedWeig
                          w1=out["1"][0], c1=out["1"][1], d1=out["1"][2], w2=w.w2, b2=w.b2)
 
 
+@dataclass
+class Ln1FoldedWeights:
+    """A layer with only LN1 folded into the QKV GEMM (sh_cuda_gemm_ln); LN2 stays a separate kernel."""
+    wqkv: int
+    cqkv: int
+    dqkv: int
+    wo: int
+    bo: int
+    w1: int
+    b1: int
+    w2: int
+    b2: int
+    g2: int
+    be2: int
+
+
+def fold_layer_norm1(rt: Runtime, w: LayerWeights, D: int) -> Ln1FoldedWeights:
+    """The LN1 half of fold_layer_norms: w' = diag(g1) wqkv, colsum = 1^T w' (fp32), bias' = be1 wqkv + bqkv."""
+    lib, a = rt.lib, rt.alloc
+    ones = a(1, D)
+    lib.sh_test_fill_const_fp16(ones, 1, D, D, 0x3C00)
+    n = 3 * D
+    wp, c, d = a(D, n), rt.alloc_bytes(4 * n), a(1, n)
+    rc = lib.sh_cuda_scale_rows(wp, w.wqkv, D, n, n, n, w.g1)
+    rc = rc or lib.sh_cuda_gemm(ones, wp, c, 1, n, D, D, n, n, 0, 0, 0, L.EPI_F32_OUT, 1)
+    rc = rc or lib.sh_cuda_gemm(w.be1, w.wqkv, d, 1, n, D, D, n, n, w.bqkv, 0, 0, L.EPI_BIAS, 1)
+    if rc:
+        raise RuntimeError(f"folding LayerNorm 1 into the QKV GEMM failed: {rc}")
+    return Ln1FoldedWeights(wqkv=wp, cqkv=c, dqkv=d, wo=w.wo, bo=w.bo, w1=w.w1, b1=w.b1, w2=w.w2, b2=w.b2, g2=w.g2,
+                            be2=w.be2)
+
+
+def layer_ops_ln1_folded(lib, act: Activations, w: Ln1FoldedWeights, stats_x: int, heads: int, eps: float,
+                         scale: float, x: int, out: int) -> list[tuple[str, Callable[[], int]]]:
+    """The 6 launches of one layer with LN1 folded into the QKV GEMM: x's row statistics are in stats_x (written by
+    the previous layer's FC2 epilogue, or sh_cuda_row_stats for the first layer), and this layer's FC2 writes those of
+    its output there for the next layer. The O projection and FC1 keep their plain epilogues (their epilogues have
+    no slack for the LayerNorm arithmetic)."""
+    B, S, D, F = act.B, act.S, act.D, act.F
+    M = B * S
+    A = L.SH_ALL
+    g = lib.sh_cuda_gemm_ln
+
+    def ln2():
+        lib.sh_layernorm(act.ln2, act.h, w.g2, w.be2, M, D, D, eps, A)
+        return 0
+
+    return [
+        ("gemm_qkv", lambda: g(x, w.wqkv, act.qkv, M, 3 * D, D, D, 3 * D, 3 * D, w.dqkv, 0, 0,
+                               L.EPI_BIAS | L.EPI_LN_IN, stats_x, w.cqkv, eps, 0)),
+        ("attention", lambda: lib.sh_cuda_attention_batched(act.qkv, act.qkv + 2 * D, act.qkv + 4 * D, act.o, S, D,
+                                                            heads, 3 * D, 3 * D, 3 * D, D, scale, B)),
+        ("gemm_o", lambda: lib.sh_cuda_gemm(act.o, w.wo, act.h, M, D, D, D, D, D, w.bo, x, D,
+                                            L.EPI_BIAS | L.EPI_RESIDUAL, 0)),
+        ("layernorm", ln2),
+        ("gemm_fc1", lambda: lib.sh_cuda_gemm(act.ln2, w.w1, act.g, M, F, D, D, F, F, w.b1, 0, 0,
+                                              L.EPI_BIAS | L.EPI_GELU, 0)),
+        ("gemm_fc2", lambda: g(act.g, w.w2, out, M, D, F, F, D, D, w.b2, act.h, D,
+                               L.EPI_BIAS | L.EPI_RESIDUAL | L.EPI_STATS_OUT, 0, 0, eps, stats_x)),
+    ]
+
+
+def encoder_schedule_ln1_folded(lib, act: Activations, layers: list[Ln1FoldedWeights], stats_x: int, heads: int,
+                                eps: float, scale: float, x_in: int | None = None,
+                                x_out: int | None = None) -> tuple[list[tuple[str, Callable[[], int]]], int]:
+    """encoder_schedule with LN1 folded: one sh_cuda_row_stats of the input, then 6 launches per layer."""
+    M, D = act.B * act.S, act.D
+    cur = act.x if x_in is None else x_in
+    nxt = act.out
+    sched = [("row_stats", lambda x0=cur: lib.sh_cuda_row_stats(x0, M, D, D, stats_x))]
+    for i, w in enumerate(layers):
+        dst = x_out if (x_out is not None and i == len(layers) - 1) else nxt
+        sched += layer_ops_ln1_folded(lib, act, w, stats_x, heads, eps, scale, cur, dst)
+        cur, nxt = dst, (act.x if nxt == act.out else act.out)
+    return sched, cur
+
+
 def alloc_row_stats(rt: Runtime, M: int, D: int) -> tuple[int, int]:
     """(stats of the residual stream x, stats of h): D / 64 fp32 (sum, sum of squares) pairs per row each."""
     return rt.alloc_bytes(M * (D // 64) * 8), rt.alloc_bytes(M * (D // 64) * 8)

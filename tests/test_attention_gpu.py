@@ -59,15 +59,16 @@ def test_attention_packed_qkv_layout(gpu_lib):
 
 
 @pytest.mark.parametrize("S,dh,H,B", [(256, 64, 12, 4), (200, 64, 2, 3), (1024, 64, 2, 1), (96, 32, 4, 2),
-                                      (128, 128, 2, 2), (52, 16, 1, 1)])
-def test_attention_batched_shapes(gpu_lib, S, dh, H, B):
+                                      (128, 128, 2, 2), (52, 16, 1, 1), (300, 64, 2, 2)])
+@pytest.mark.parametrize("sign", [1.0, -1.0])
+def test_attention_batched_shapes(gpu_lib, S, dh, H, B, sign):
     rt, lib = gpu_lib, gpu_lib.lib
     rt.reset()
     D = dh * H
     q, k, v = (lcg.normal_fp16(B * S, D, s) for s in (1, 2, 3))
     dq, dk, dv = rt.upload(q), rt.upload(k), rt.upload(v)
     do = rt.alloc(B * S, D)
-    scale = 1.0 / np.sqrt(dh)
+    scale = sign / np.sqrt(dh)
     assert lib.sh_cuda_attention_batched(dq, dk, dv, do, S, D, H, D, D, D, D, scale, B) == 0
     rt.check()
     got = rt.get(do, B * S, D)
@@ -75,6 +76,31 @@ def test_attention_batched_shapes(gpu_lib, S, dh, H, B):
         sl = slice(b * S, (b + 1) * S)
         want = ops.attention(q[sl], k[sl], v[sl], H, scale, rounding=False)
         err, rel = ops.max_abs_and_rel_l2(got[sl], want)
+        assert err <= 2e-2 and rel <= 5e-3, (b, err, rel)
+
+
+@pytest.mark.parametrize("S,H,B,scale", [(132, 3, 2, 0.125), (4, 1, 3, 0.125), (256, 12, 2, -0.125),
+                                          (200, 2, 2, -0.3), (128, 4, 3, 0.125)])
+def test_attention_single_block_cases(gpu_lib, S, H, B, scale):
+    """Edge cases of the tensor-core kernel at S <= 256: a second query tile with 4 valid rows and 4 valid keys in
+    the second key block (S = 132), tiny S, a negative softmax scale (the row max of s * scale is the minimum of s,
+    and masked keys must still get p = 0), and one query tile only (S = 128); nothing is written outside the output
+    columns."""
+    rt, lib = gpu_lib, gpu_lib.lib
+    rt.reset()
+    D = 64 * H
+    q, k, v = (lcg.normal_fp16(B * S, D, s) for s in (31, 32, 33))
+    dq, dk, dv = rt.upload(q), rt.upload(k), rt.upload(v)
+    do = rt.alloc(B * S, D + 64)
+    rt.view(do, B * S, D + 64).fill_(3.0)
+    assert lib.sh_cuda_attention_batched(dq, dk, dv, do, S, D, H, D, D, D, D + 64, scale, B) == 0
+    rt.check()
+    got = rt.get(do, B * S, D + 64)
+    assert (got[:, D:] == 3.0).all()              # nothing written outside the output columns
+    for b in range(B):
+        sl = slice(b * S, (b + 1) * S)
+        want = ops.attention(q[sl], k[sl], v[sl], H, scale, rounding=False)
+        err, rel = ops.max_abs_and_rel_l2(got[sl, :D], want)
         assert err <= 2e-2 and rel <= 5e-3, (b, err, rel)
 
 

@@ -38,12 +38,14 @@ def _oracle_params(layer: int) -> dict[str, np.ndarray]:
     return p, wqkv
 
 
-def test_encoder_config5_matches_fp32_oracle(gpu_lib):
+@pytest.mark.parametrize("fold", ["none", "ln1"])
+def test_encoder_config5_matches_fp32_oracle(gpu_lib, fold):
+    """fold = "ln1": LN1 folded into the QKV GEMM (bench.py --ln-fold ln1), row statistics from FC2's epilogue."""
     import torch
 
     from softhier_cuda.runtime import Runtime
     M = B * S
-    arena = (11 * M * D + M * F + LAYERS * (7 * D * D + 3 * D * F + 16 * F)) * 2 + (64 << 20)
+    arena = (11 * M * D + M * F + LAYERS * (7 * D * D + 3 * D * F + 16 * F)) * 2 + (160 << 20)
     rt = Runtime(0, arena)          # its own arena; gpu_lib's is bound again at the end
     try:
         lib = rt.lib
@@ -71,8 +73,14 @@ def test_encoder_config5_matches_fp32_oracle(gpu_lib):
         cur, nxt = x_in, act.out
         ref = {b: xs[b].astype(np.float32) for b in SAMPLED}
         growth = []
+        if fold == "ln1":
+            folded = [encoder.fold_layer_norm1(rt, w, D) for w in layers]
+            stats_x = encoder.alloc_row_stats(rt, M, D)[0]
+            assert lib.sh_cuda_row_stats(x_in, M, D, D, stats_x) == 0
         for li, w in enumerate(layers):
-            for kind, fn in encoder.layer_ops(lib, act, w, H, EPS, SCALE, cur, nxt):
+            ops_l = (encoder.layer_ops(lib, act, w, H, EPS, SCALE, cur, nxt) if fold == "none" else
+                     encoder.layer_ops_ln1_folded(lib, act, folded[li], stats_x, H, EPS, SCALE, cur, nxt))
+            for kind, fn in ops_l:
                 assert fn() == 0, (li, kind)
             rt.check()
             errs = []

@@ -204,10 +204,15 @@ def test_fp32_carried_k_split(gpu_lib):
 @pytest.mark.parametrize("M,N,K,flags", [(8192, 768, 768, 0), (8192, 2304, 768, L.EPI_BIAS),
                                          (8000, 768, 3072, L.EPI_BIAS | L.EPI_RESIDUAL),
                                          (8192, 3072, 768, L.EPI_BIAS | L.EPI_GELU), (9984, 1024, 640, 0),
-                                         (2816, 4096, 256, L.EPI_BIAS)])
+                                         (2816, 4096, 256, L.EPI_BIAS),
+                                         (6400, 768, 768, L.EPI_BIAS | L.EPI_RESIDUAL),
+                                         (8192, 768, 768, L.EPI_ACCUMULATE | L.EPI_BIAS | L.EPI_RESIDUAL),
+                                         (7936, 1536, 512, L.EPI_RESIDUAL)])
 def test_pair_tiles(gpu_lib, M, N, K, flags):
     """Shapes with enough 256 x 256 tiles run on the 2-CTA (cta_group::2) kernel. 9984 and 2816 rows (39 and 11
-    row-tiles) end with a partial group of the grouped tile order, 2816 x 4096 with 16 column-tiles per row."""
+    row-tiles) end with a partial group of the grouped tile order, 2816 x 4096 with 16 column-tiles per row. With a
+    residual the residual tile is written into the accumulator before the MMAs: 8000 rows end in a partial row-tile,
+    6400 x 768 (75 tiles on 74 SM pairs) leaves most pairs a single tile, and accumulate adds Z on top."""
     got, want = _run(gpu_lib, M, N, K, flags=flags)
     _close(got, want, K)
 
