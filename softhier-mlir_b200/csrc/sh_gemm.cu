@@ -741,6 +741,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     } else if (warp == 1) {
         if (lane == 0 && leader) {
             constexpr uint32_t idesc = umma_idesc_f16(256, C::kMmaN, 0, 1);
+            constexpr uint32_t NH = BN / C::kMmaN;
+            // The issue loop is one thread's dependency chain, so it does as little as possible per MMA: the
+            // descriptors of stage 0 are built once and a stage / k-step only adds its offset / 16 to the 14-bit
+            // address field (shared-memory offsets stay below 256 KB, so the sum never carries out of the field);
+            // the stage barriers' cluster addresses are those of stage 0 plus 8 bytes per stage.
+            const uint64_t a_desc0 = sw128_desc(smem_u32(smem), 16, 1024);
+            const uint64_t b_desc0 = sw128_desc(smem_u32(smem) + C::kABytes, BK * 128, 1024);
+            const uint32_t empty_r0 = mapa_shared(smem_u32(&empty[0]), 0), empty_r1 = mapa_shared(smem_u32(&empty[0]), 1);
             uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
             bool ok = true;
             for (uint32_t u = pair; ok && u < total_units; u += npairs) {
@@ -755,17 +763,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t sa = smem_u32(smem + stage * C::kStageBytes);
-                    const uint32_t sb = sa + C::kABytes;
+                    const uint64_t so = (stage * C::kStageBytes) >> 4;
+                    const uint64_t ad = a_desc0 + so, bd = b_desc0 + so;
 #pragma unroll
                     for (int j = 0; j < BK / 16; ++j)
 #pragma unroll
-                        for (uint32_t h = 0; h < BN / C::kMmaN; ++h)
-                            if (h >= h0 && h < h0 + nh)
-                            umma_f16_ss_pair(d + h * C::kMmaN, sw128_desc(sa + j * 32, 16, 1024),
-                                             sw128_desc(sb + h * (C::kMmaN / 2) * BK * 2 + j * 2048, BK * 128, 1024),
-                                             idesc, (kb > 0 || j > 0) ? 1u : 0u);
-                    umma_commit_pair_both(&empty[stage]);
+                        for (uint32_t h = 0; h < NH; ++h)
+                            if (NH == 1 || (h >= h0 && h < h0 + nh))
+                                umma_f16_ss_pair(d + h * C::kMmaN, ad + (uint64_t)(j * 2),
+                                                 bd + (uint64_t)((h * (C::kMmaN / 2) * BK * 2 + j * 2048) >> 4), idesc,
+                                                 (kb > 0 || j > 0) ? 1u : 0u);
+                    umma_commit_pair_to(empty_r0 + stage * 8u);
+                    umma_commit_pair_to(empty_r1 + stage * 8u);
                     if (++stage == S) {
                         stage = 0;
                         phase ^= 1u;

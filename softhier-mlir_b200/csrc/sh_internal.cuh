@@ -358,6 +358,12 @@ __device__ __forceinline__ void umma_commit_pair_both(uint64_t *bar) {
                      : "memory");
 }
 
+// Commit of the leader's MMAs to the barrier at a shared::cluster address (one CTA of the pair).
+__device__ __forceinline__ void umma_commit_pair_to(uint32_t cluster_addr) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(cluster_addr)
+                 : "memory");
+}
+
 // D (+)= A . B with A (M x K, K-major, two fp16 per 32-bit column) read from tensor memory, B from shared memory.
 __device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
                                             uint32_t accumulate) {
