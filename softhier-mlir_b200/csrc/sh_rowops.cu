@@ -49,11 +49,36 @@ __device__ __forceinline__ float warp_max(float v) {
 }
 
 // ---- layernorm (optionally fused with the residual add h = a + b) -------------------------------------
+// The row stays in registers as fp16 (4 registers per 8 columns) and is converted on each of the three uses, so the
+// kernel fits 40 registers and 6 blocks (48 rows in flight) per SM for rows up to 1024 columns: more loads in
+// flight, which matters where the power cap holds the SM clock low.
+__device__ __forceinline__ float sum8(const uint4 &raw) {
+    const __half2 *h = reinterpret_cast<const __half2 *>(&raw);
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float2 f = __half22float2(h[i]);
+        s += f.x + f.y;
+    }
+    return s;
+}
+__device__ __forceinline__ float sqdev8(const uint4 &raw, float mean) {
+    const __half2 *h = reinterpret_cast<const __half2 *>(&raw);
+    float q = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float2 f = __half22float2(h[i]);
+        q = fmaf(f.x - mean, f.x - mean, q);
+        q = fmaf(f.y - mean, f.y - mean, q);
+    }
+    return q;
+}
+
 template <int VPL, bool ADD>
-__global__ void __launch_bounds__(kWarpsPerBlock * 32) k_layernorm_vec(__half *y, __half *h, const __half *a,
-                                                                       const __half *b, const __half *g,
-                                                                       const __half *be, uint32_t rows, uint32_t cols,
-                                                                       uint32_t ld, float eps) {
+__global__ void __launch_bounds__(kWarpsPerBlock * 32, VPL <= 4 ? 6 : 1) k_layernorm_vec(__half *y, __half *h, const __half *a,
+                                                                          const __half *b, const __half *g,
+                                                                          const __half *be, uint32_t rows,
+                                                                          uint32_t cols, uint32_t ld, float eps) {
     pdl_launch_dependents();
     pdl_wait();
     const uint32_t lane = threadIdx.x & 31;
@@ -61,45 +86,56 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) k_layernorm_vec(__half *y
     if (row >= rows) return;
     const uint32_t cv = cols >> 3;
     const __half *ar = a + (size_t)row * ld;
-    Vec8 x[VPL];
-    float s = 0.f;
+    uint4 x[VPL];
 #pragma unroll
     for (int i = 0; i < VPL; ++i) {
         const uint32_t v = lane + 32 * i;
-        if (v < cv) {
-            x[i] = load8(ar + 8 * v);
-            if (ADD) {
-                Vec8 bb = load8(b + (size_t)row * ld + 8 * v);
+        x[i] = make_uint4(0u, 0u, 0u, 0u);
+        if (v < cv) x[i] = *reinterpret_cast<const uint4 *>(ar + 8 * v);
+    }
+    if (ADD) {   // h = fp16(a + b), stored, and normalised below
 #pragma unroll
-                for (int j = 0; j < 8; ++j) x[i].v[j] = __half2float(__float2half_rn(x[i].v[j] + bb.v[j]));
-                store8(h + (size_t)row * ld + 8 * v, x[i]);
+        for (int i = 0; i < VPL; ++i) {
+            const uint32_t v = lane + 32 * i;
+            if (v < cv) {
+                const uint4 bb = *reinterpret_cast<const uint4 *>(b + (size_t)row * ld + 8 * v);
+                __half2 *xh = reinterpret_cast<__half2 *>(&x[i]);
+                const __half2 *bh = reinterpret_cast<const __half2 *>(&bb);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const float2 fa = __half22float2(xh[j]), fb = __half22float2(bh[j]);
+                    xh[j] = __floats2half2_rn(fa.x + fb.x, fa.y + fb.y);
+                }
+                *reinterpret_cast<uint4 *>(h + (size_t)row * ld + 8 * v) = x[i];
             }
-#pragma unroll
-            for (int j = 0; j < 8; ++j) s += x[i].v[j];
         }
     }
-    const float mean = warp_sum(s) / (float)cols;
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) s += sum8(x[i]);   // zero vectors past the row add nothing
+    const float inv_cols = 1.f / (float)cols;
+    const float mean = warp_sum(s) * inv_cols;
     float q = 0.f;
 #pragma unroll
-    for (int i = 0; i < VPL; ++i) {
-        if (lane + 32 * i < cv) {
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const float d = x[i].v[j] - mean;
-                q += d * d;
-            }
-        }
-    }
-    const float rstd = rsqrtf(warp_sum(q) / (float)cols + eps);
+    for (int i = 0; i < VPL; ++i)
+        if (lane + 32 * i < cv) q += sqdev8(x[i], mean);
+    const float rstd = rsqrtf(warp_sum(q) * inv_cols + eps);
     __half *yr = y + (size_t)row * ld;
 #pragma unroll
     for (int i = 0; i < VPL; ++i) {
         const uint32_t v = lane + 32 * i;
         if (v < cv) {
-            Vec8 gg = load8(g + 8 * v), bb = load8(be + 8 * v), o;
+            const uint4 gr = *reinterpret_cast<const uint4 *>(g + 8 * v), br = *reinterpret_cast<const uint4 *>(be + 8 * v);
+            const __half2 *xh = reinterpret_cast<const __half2 *>(&x[i]), *gh = reinterpret_cast<const __half2 *>(&gr),
+                          *bh = reinterpret_cast<const __half2 *>(&br);
+            uint4 o;
+            __half2 *oh = reinterpret_cast<__half2 *>(&o);
 #pragma unroll
-            for (int j = 0; j < 8; ++j) o.v[j] = (x[i].v[j] - mean) * rstd * gg.v[j] + bb.v[j];
-            store8(yr + 8 * v, o);
+            for (int j = 0; j < 4; ++j) {
+                const float2 fx = __half22float2(xh[j]), fg = __half22float2(gh[j]), fb = __half22float2(bh[j]);
+                oh[j] = __floats2half2_rn((fx.x - mean) * rstd * fg.x + fb.x, (fx.y - mean) * rstd * fg.y + fb.y);
+            }
+            *reinterpret_cast<uint4 *>(yr + 8 * v) = o;
         }
     }
 }
