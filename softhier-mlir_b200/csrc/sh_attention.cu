@@ -390,9 +390,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             bool have_prev = false, prev_first = false;
             uint32_t prev_st = 0, prev_ph = 0, prev_g = 0;
             bool ok = true;
+            // descriptors built once; a stage / slot / k-step adds its byte offset / 16 to the 14-bit address field
+            // (shared-memory offsets stay below 256 KB, so the sum never carries out of the field)
+            const uint64_t kv_desc0 = sw128_desc(smem_u32(sm + kKvOff), 16, 1024);                 // K, stage 0
+            const uint64_t v_desc0 = sw128_desc(smem_u32(sm + kKvOff + kTileBytes), 16384, 1024);  // V, stage 0
+            const uint64_t q_desc0 = sw128_desc(smem_u32(sm + kQOff), 16, 1024);                   // Q, slot 0
             auto issue_pv = [&](uint32_t pst, uint32_t pph, uint32_t pg, bool first) -> bool {
                 if (!mbar_wait(&v_full[pst], pph, abort, a.err)) return false;
-                const uint32_t av = smem_u32(sm + kKvOff + pst * 2 * kTileBytes + kTileBytes);
+                const uint64_t vd = v_desc0 + ((pst * 2 * kTileBytes) >> 4);
 #pragma unroll 1
                 for (uint32_t t = 0; t < 2; ++t) {
                     if (!mbar_wait(&p_full[t], pg & 1u, abort, a.err)) return false;
@@ -401,14 +406,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 #pragma unroll
                     for (int k = 0; k < kTcKeys / 16; ++k)
                         umma_f16_ts(tmem + kTmO + t * kTcDh, tmem + kTmP + t * (kTcKeys / 2) + k * 8,
-                                    sw128_desc(av + k * 2048, 16384, 1024), idesc_o, (first && k == 0) ? 0u : 1u);
+                                    vd + (uint64_t)(k * (2048 >> 4)), idesc_o, (first && k == 0) ? 0u : 1u);
                     umma_commit(&o_full[t]);
                 }
                 umma_commit(&kv_empty[pst]);
                 return true;
             };
             for (uint32_t it = blockIdx.x; ok && it < a.items; it += gridDim.x) {
-                const uint32_t aq = smem_u32(sm + kQOff + qs * 2 * kTileBytes);
+                const uint64_t qd = q_desc0 + ((qs * 2 * kTileBytes) >> 4);
                 for (uint32_t j = 0; j < a.nkb; ++j) {
                     // at an item boundary the previous item's last P V goes first: its softmax waits on it to finish
                     // the item, while the new item's scores are not needed before that
@@ -424,7 +429,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                         ok = false;
                         break;
                     }
-                    const uint32_t ak = smem_u32(sm + kKvOff + st * 2 * kTileBytes);
+                    const uint64_t kd = kv_desc0 + ((st * 2 * kTileBytes) >> 4);
 #pragma unroll 1
                     for (uint32_t t = 0; t < 2 && ok; ++t) {
                         // the softmax of tile t has its previous scores in registers
@@ -435,8 +440,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                         tc_fence_after();
 #pragma unroll
                         for (int k = 0; k < kTcDh / 16; ++k)
-                            umma_f16_ss(tmem + kTmS + t * kTcKeys, sw128_desc(aq + t * kTileBytes + k * 32, 16, 1024),
-                                        sw128_desc(ak + k * 32, 16, 1024), idesc_s, k > 0 ? 1u : 0u);
+                            umma_f16_ss(tmem + kTmS + t * kTcKeys, qd + (uint64_t)((t * kTileBytes + k * 32) >> 4),
+                                        kd + (uint64_t)(k * 2), idesc_s, k > 0 ? 1u : 0u);
                         umma_commit(&s_full[t]);
                     }
                     if (!ok) break;
