@@ -431,6 +431,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
             // ---------------- MMA issuer ----------------
             constexpr uint32_t idesc = umma_idesc_f16(BM, BN, 0, 1);
+            // descriptors of stage 0 built once; a stage / k-step adds its byte offset / 16 to the 14-bit address
+            // field (shared-memory offsets stay below 256 KB, so the sum never carries out of the field)
+            const uint64_t a_desc0 = sw128_desc(smem_u32(smem), 16, 1024);
+            const uint64_t b_desc0 = sw128_desc(smem_u32(smem) + C::kABytes, BK * 128, 1024);
             uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
             bool ok = true;
             for (uint32_t u = blockIdx.x; ok && u < total_units; u += gridDim.x) {
@@ -447,14 +451,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t sa = smem_u32(smem + stage * C::kStageBytes);
-                    const uint32_t sb = sa + C::kABytes;
+                    const uint64_t so = (stage * C::kStageBytes) >> 4;
 #pragma unroll
-                    for (int j = 0; j < BK / 16; ++j) {
-                        const uint64_t ad = sw128_desc(sa + j * 32, 16, 1024);
-                        const uint64_t bd = sw128_desc(sb + j * 2048, BK * 128, 1024);
-                        umma_f16_ss(d, ad, bd, idesc, (kb > kb0 || j > 0) ? 1u : 0u);
-                    }
+                    for (int j = 0; j < BK / 16; ++j)
+                        umma_f16_ss(d, a_desc0 + so + (uint64_t)(j * 2), b_desc0 + so + (uint64_t)(j * (2048 >> 4)),
+                                    idesc, (kb > kb0 || j > 0) ? 1u : 0u);
                     umma_commit(&empty[stage]);
                     if (++stage == S) {
                         stage = 0;
