@@ -740,7 +740,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                 if (armed[s] != 2) drain_wait(&empty[s], armed[s]);
         }
     } else if (warp == 1) {
-        if (lane == 0 && leader) {
+        if (leader) {   // the whole warp walks the loop; lane 0 issues (is0)
+            const uint32_t is0 = lane == 0 ? 1u : 0u;
             constexpr uint32_t idesc = umma_idesc_f16(256, C::kMmaN, 0, 1);
             constexpr uint32_t NH = BN / C::kMmaN;
             // The issue loop is one thread's dependency chain, so it does as little as possible per MMA: the
@@ -771,24 +772,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
 #pragma unroll
                         for (uint32_t h = 0; h < NH; ++h)
                             if (NH == 1 || (h >= h0 && h < h0 + nh))
-                                umma_f16_ss_pair(d + h * C::kMmaN, ad + (uint64_t)(j * 2),
-                                                 bd + (uint64_t)((h * (C::kMmaN / 2) * BK * 2 + j * 2048) >> 4), idesc,
-                                                 (kb > 0 || j > 0) ? 1u : 0u);
-                    umma_commit_pair_to(empty_r0 + stage * 8u);
-                    umma_commit_pair_to(empty_r1 + stage * 8u);
+                                umma_f16_ss_pair_if(is0, d + h * C::kMmaN, ad + (uint64_t)(j * 2),
+                                                    bd + (uint64_t)((h * (C::kMmaN / 2) * BK * 2 + j * 2048) >> 4),
+                                                    idesc, (kb > 0 || j > 0) ? 1u : 0u);
+                    umma_commit_pair_to_if(is0, empty_r0 + stage * 8u);
+                    umma_commit_pair_to_if(is0, empty_r1 + stage * 8u);
                     if (++stage == S) {
                         stage = 0;
                         phase ^= 1u;
                     }
                 }
                 if (!ok) break;
-                umma_commit_pair_both(&tfull[acc]);
+                if (is0) umma_commit_pair_both(&tfull[acc]);
                 if (++acc == C::kAcc) {
                     acc = 0;
                     acc_phase ^= 1u;
                 }
             }
-            umma_commit_pair_both(mdone);   // both CTAs: every MMA the leader issued has completed
+            if (is0) umma_commit_pair_both(mdone);   // both CTAs: every MMA the leader issued has completed
         }
         if (lane == 0) drain_wait(mdone, 0);
     } else if (warp == 10) {

@@ -358,6 +358,26 @@ __device__ __forceinline__ void umma_commit_pair_both(uint64_t *bar) {
                      : "memory");
 }
 
+// The pair MMA and commit issued only where `issue` is nonzero: the whole warp walks the issue loop (warp-uniform
+// control flow and operands) and one lane issues, without a branch per instruction.
+__device__ __forceinline__ void umma_f16_ss_pair_if(uint32_t issue, uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                                    uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "setp.ne.b32 q, %5, 0;\n\t"
+        "@q tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(issue)
+        : "memory");
+}
+__device__ __forceinline__ void umma_commit_pair_to_if(uint32_t issue, uint32_t cluster_addr) {
+    asm volatile(
+        "{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %1, 0;\n\t"
+        "@q tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(cluster_addr),
+        "r"(issue)
+        : "memory");
+}
+
 // Commit of the leader's MMAs to the barrier at a shared::cluster address (one CTA of the pair).
 __device__ __forceinline__ void umma_commit_pair_to(uint32_t cluster_addr) {
     asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(cluster_addr)
