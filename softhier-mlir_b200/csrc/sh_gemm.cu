@@ -428,8 +428,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (armed[s] != 2) drain_wait(&full[s], armed[s]);
         }
     } else if (warp == 1) {
-        if (lane == 0) {
-            // ---------------- MMA issuer ----------------
+        {
+            // ---------------- MMA issuer: the whole warp walks the loop, lane 0 issues (is0) ----------------
+            const uint32_t is0 = lane == 0 ? 1u : 0u;
             constexpr uint32_t idesc = umma_idesc_f16(BM, BN, 0, 1);
             // descriptors of stage 0 built once; a stage / k-step adds its byte offset / 16 to the 14-bit address
             // field (shared-memory offsets stay below 256 KB, so the sum never carries out of the field)
@@ -454,22 +455,22 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint64_t so = (stage * C::kStageBytes) >> 4;
 #pragma unroll
                     for (int j = 0; j < BK / 16; ++j)
-                        umma_f16_ss(d, a_desc0 + so + (uint64_t)(j * 2), b_desc0 + so + (uint64_t)(j * (2048 >> 4)),
-                                    idesc, (kb > kb0 || j > 0) ? 1u : 0u);
-                    umma_commit(&empty[stage]);
+                        umma_f16_ss_if(is0, d, a_desc0 + so + (uint64_t)(j * 2),
+                                       b_desc0 + so + (uint64_t)(j * (2048 >> 4)), idesc, (kb > kb0 || j > 0) ? 1u : 0u);
+                    umma_commit_if(is0, &empty[stage]);
                     if (++stage == S) {
                         stage = 0;
                         phase ^= 1u;
                     }
                 }
                 if (!ok) break;
-                umma_commit(&tfull[acc]);
+                umma_commit_if(is0, &tfull[acc]);
                 acc ^= 1u;
                 if (acc == 0) acc_phase ^= 1u;
             }
             // exit path: tensor memory may only be freed once every issued MMA has completed
-            umma_commit(mdone);
-            drain_wait(mdone, 0);
+            umma_commit_if(is0, mdone);
+            if (is0) drain_wait(mdone, 0);
         }
     } else {
         // ---------------- epilogue (warps 2..9) ----------------

@@ -370,6 +370,23 @@ __device__ __forceinline__ void umma_f16_ss_pair_if(uint32_t issue, uint32_t d_t
         "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(issue)
         : "memory");
 }
+__device__ __forceinline__ void umma_f16_ss_if(uint32_t issue, uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                               uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "setp.ne.b32 q, %5, 0;\n\t"
+        "@q tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(issue)
+        : "memory");
+}
+__device__ __forceinline__ void umma_commit_if(uint32_t issue, uint64_t *bar) {
+    asm volatile(
+        "{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %1, 0;\n\t"
+        "@q tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(smem_u32(bar)),
+        "r"(issue)
+        : "memory");
+}
 __device__ __forceinline__ void umma_commit_pair_to_if(uint32_t issue, uint32_t cluster_addr) {
     asm volatile(
         "{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %1, 0;\n\t"
