@@ -381,8 +381,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                 }
         }
     } else if (warp == 1) {
-        if (lane == 0) {
-            // ---------------- MMA issuer ----------------
+        {
+            // ---------------- MMA issuer: the whole warp walks the loop, lane 0 issues (is0) ----------------
+            const uint32_t is0 = lane == 0 ? 1u : 0u;
             constexpr uint32_t idesc_s = umma_idesc_f16(kTcRows, kTcKeys, 0, 0);
             constexpr uint32_t idesc_o = umma_idesc_f16(kTcRows, kTcDh, 0, 1);
             uint32_t qs = 0, qph = 0, st = 0, kph = 0, g = 0;
@@ -405,11 +406,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                     // P_t (128 x 128 keys) from tensor memory: 16 keys = 8 columns per MMA
 #pragma unroll
                     for (int k = 0; k < kTcKeys / 16; ++k)
-                        umma_f16_ts(tmem + kTmO + t * kTcDh, tmem + kTmP + t * (kTcKeys / 2) + k * 8,
-                                    vd + (uint64_t)(k * (2048 >> 4)), idesc_o, (first && k == 0) ? 0u : 1u);
-                    umma_commit(&o_full[t]);
+                        umma_f16_ts_if(is0, tmem + kTmO + t * kTcDh, tmem + kTmP + t * (kTcKeys / 2) + k * 8,
+                                       vd + (uint64_t)(k * (2048 >> 4)), idesc_o, (first && k == 0) ? 0u : 1u);
+                    umma_commit_if(is0, &o_full[t]);
                 }
-                umma_commit(&kv_empty[pst]);
+                umma_commit_if(is0, &kv_empty[pst]);
                 return true;
             };
             for (uint32_t it = blockIdx.x; ok && it < a.items; it += gridDim.x) {
@@ -440,12 +441,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                         tc_fence_after();
 #pragma unroll
                         for (int k = 0; k < kTcDh / 16; ++k)
-                            umma_f16_ss(tmem + kTmS + t * kTcKeys, qd + (uint64_t)((t * kTileBytes + k * 32) >> 4),
-                                        kd + (uint64_t)(k * 2), idesc_s, k > 0 ? 1u : 0u);
-                        umma_commit(&s_full[t]);
+                            umma_f16_ss_if(is0, tmem + kTmS + t * kTcKeys,
+                                           qd + (uint64_t)((t * kTileBytes + k * 32) >> 4), kd + (uint64_t)(k * 2),
+                                           idesc_s, k > 0 ? 1u : 0u);
+                        umma_commit_if(is0, &s_full[t]);
                     }
                     if (!ok) break;
-                    if (j + 1 == a.nkb) umma_commit(&q_empty[qs]);   // Q slot free once these MMAs complete
+                    if (j + 1 == a.nkb) umma_commit_if(is0, &q_empty[qs]);   // Q slot free once these MMAs complete
                     if (have_prev && !issue_pv(prev_st, prev_ph, prev_g, prev_first)) {
                         ok = false;
                         break;
@@ -468,8 +470,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             }
             if (ok && have_prev) issue_pv(prev_st, prev_ph, prev_g, prev_first);
             // exit path: tensor memory may only be freed once every issued MMA has completed
-            umma_commit(&mdone[0]);
-            drain_wait(&mdone[0], 0);
+            umma_commit_if(is0, &mdone[0]);
+            if (is0) drain_wait(&mdone[0], 0);
         }
     } else {
         // ---------------- softmax + output (warps 2..5: tile 0, warps 6..9: tile 1) ----------------
