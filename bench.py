@@ -638,14 +638,23 @@ def run_gemm(args, local: int) -> dict:
             if call():
                 raise RuntimeError(lib.sh_cuda_last_error_string().decode())
         rt.check()
+        clocks = ClockSampler(local)
+        clocks.start()
+        torch.cuda.synchronize()
+        clocks.mark()
         ms = _event_time(torch, stream, call, max(1, args.steps))
+        clock_info = clocks.stop()
     rt.check()
     flop = 2.0 * M * N * K
     pk, src = peaks()
     tf = flop / ms / 1e9
+    # tensor work per SM clock: 8192 fp16 FLOP / clk / SM is the dense tcgen05 rate
+    per_clk = (tf * 1e12 / (torch.cuda.get_device_properties(local).multi_processor_count * clock_info["sm_mhz"] * 1e6)
+               if clock_info.get("sm_mhz") else None)
     out = {"metric": "GEMM TFLOP/s", "value": round(tf, 1), "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps,
            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "dtype": "f16",
            "frac_of_peak": round(tf / pk["bf16_tflops"], 4), "peak": f"{src} bf16 burst {pk['bf16_tflops']} TFLOP/s",
+           "clocks": clock_info, "frac_of_clock_peak": round(per_clk / 8192, 4) if per_clk else None,
            "config": {"workload": f"sh_cuda_gemm {M}x{N}x{K} epilogue [{args.epi}]",
                       "l2": "Z alone larger than L2 at the default shape; no flush"}}
     if args.vs_cublas:

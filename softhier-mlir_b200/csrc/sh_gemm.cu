@@ -748,10 +748,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
             // The issue loop is one thread's dependency chain, so it does as little as possible per MMA: the
             // descriptors of stage 0 are built once and a stage / k-step only adds its offset / 16 to the 14-bit
             // address field (shared-memory offsets stay below 256 KB, so the sum never carries out of the field);
-            // the stage barriers' cluster addresses are those of stage 0 plus 8 bytes per stage.
+            // one commit per k-step frees the stage in both CTAs.
             const uint64_t a_desc0 = sw128_desc(smem_u32(smem), 16, 1024);
             const uint64_t b_desc0 = sw128_desc(smem_u32(smem) + C::kABytes, BK * 128, 1024);
-            const uint32_t empty_r0 = mapa_shared(smem_u32(&empty[0]), 0), empty_r1 = mapa_shared(smem_u32(&empty[0]), 1);
             uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
             bool ok = true;
             for (uint32_t u = pair; ok && u < total_units; u += npairs) {
@@ -776,15 +775,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                                 umma_f16_ss_pair_if(is0, d + h * C::kMmaN, ad + (uint64_t)(j * 2),
                                                     bd + (uint64_t)((h * (C::kMmaN / 2) * BK * 2 + j * 2048) >> 4),
                                                     idesc, (kb > 0 || j > 0) ? 1u : 0u);
-                    umma_commit_pair_to_if(is0, empty_r0 + stage * 8u);
-                    umma_commit_pair_to_if(is0, empty_r1 + stage * 8u);
+                    umma_commit_pair_mask_if(is0, &empty[stage], 0x3);
                     if (++stage == S) {
                         stage = 0;
                         phase ^= 1u;
                     }
                 }
                 if (!ok) break;
-                if (is0) umma_commit_pair_both(&tfull[acc]);
+                umma_commit_pair_mask_if(is0, &tfull[acc], 0x3);
                 if (++acc == C::kAcc) {
                     acc = 0;
                     acc_phase ^= 1u;

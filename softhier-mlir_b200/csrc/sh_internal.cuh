@@ -358,6 +358,18 @@ __device__ __forceinline__ void umma_commit_pair_both(uint64_t *bar) {
                      : "memory");
 }
 
+// One commit that arrives on the barrier at this shared-memory offset in every CTA of `cta_mask` (0b11: both CTAs
+// of the pair) when the leader's MMAs issued so far are complete. This is the commit's own cluster signal, not a
+// memory load.
+__device__ __forceinline__ void umma_commit_pair_mask_if(uint32_t issue, uint64_t *bar, uint16_t cta_mask) {
+    asm volatile(
+        "{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %2, 0;\n\t"
+        "@q tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;\n\t}" ::"r"(
+            smem_u32(bar)),
+        "h"(cta_mask), "r"(issue)
+        : "memory");
+}
+
 // The pair MMA and commit issued only where `issue` is nonzero: the whole warp walks the issue loop (warp-uniform
 // control flow and operands) and one lane issues, without a branch per instruction.
 __device__ __forceinline__ void umma_f16_ss_pair_if(uint32_t issue, uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
@@ -386,19 +398,6 @@ __device__ __forceinline__ void umma_commit_if(uint32_t issue, uint64_t *bar) {
         "@q tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(smem_u32(bar)),
         "r"(issue)
         : "memory");
-}
-__device__ __forceinline__ void umma_commit_pair_to_if(uint32_t issue, uint32_t cluster_addr) {
-    asm volatile(
-        "{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %1, 0;\n\t"
-        "@q tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(cluster_addr),
-        "r"(issue)
-        : "memory");
-}
-
-// Commit of the leader's MMAs to the barrier at a shared::cluster address (one CTA of the pair).
-__device__ __forceinline__ void umma_commit_pair_to(uint32_t cluster_addr) {
-    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(cluster_addr)
-                 : "memory");
 }
 
 // D (+)= A . B with A (M x K, K-major, two fp16 per 32-bit column) read from tensor memory, B from shared memory.
