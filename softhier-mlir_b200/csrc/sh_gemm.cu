@@ -643,16 +643,19 @@ __device__ __forceinline__ void pair_unit(const GemmArgs &a, uint32_t u, uint32_
     }
 }
 
-template <int BN, bool RES = false>
+// KS = 2: the stages go in pairs that share one full / empty barrier, so the producer waits, arms and the MMA
+// thread waits, fences and commits once per two k-steps (the k-block count of every tile must be even).
+template <int BN, bool RES = false, int KS = 1>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     k_gemm_tc2(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w,
                const __grid_constant__ CUtensorMap map_z, const __grid_constant__ CUtensorMap map_r, GemmArgs a) {
     using C = PairCfg<BN, RES>;
-    constexpr int S = C::kStages;
+    static_assert(C::kStages % KS == 0, "stage groups");
+    constexpr int S = C::kStages / KS;   // barrier groups of KS stages
     extern __shared__ uint8_t smem_raw[];
     const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
     uint8_t *smem = smem_raw + pad;
-    uint8_t *epi_stage = smem + S * C::kStageBytes;
+    uint8_t *epi_stage = smem + C::kStages * C::kStageBytes;
     uint64_t *full = reinterpret_cast<uint64_t *>(epi_stage + C::kEpiBytes);
     uint64_t *empty = full + S;
     uint64_t *tfull = empty + S;
@@ -708,27 +711,31 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                 pair_unit<BN>(a, u, tile, h0, nh);
                 tile_coords(tile, a.num_tiles / a.tiles_n, a.tiles_n, a.group_m, tm, tn);
                 const uint32_t stage_tx = 2 * (C::kABytes + nh * (C::kMmaN / 2) * BK * 2);   // both CTAs' bytes
-                for (uint32_t kb = 0; kb < a.k_blocks; ++kb) {
+                for (uint32_t kb = 0; kb < a.k_blocks; kb += KS) {
                     if (!mbar_wait(&empty[stage], phase ^ 1u, abort, a.err)) {
                         ok = false;
                         break;
                     }
-                    uint8_t *sa = smem + stage * C::kStageBytes;
-                    uint8_t *sb = sa + C::kABytes;
                     const uint32_t bar = mapa_shared(smem_u32(&full[stage]), 0);
-                    if (leader) mbar_arrive_expect_tx(&full[stage], stage_tx);
+                    if (leader) mbar_arrive_expect_tx(&full[stage], KS * stage_tx);
                     armed[stage] = phase;
-                    tma_load_2d_pair(sa, &map_x, bar, (int32_t)(kb * BK), (int32_t)(tm * 256 + rank * 128));
-                    // 64-column boxes: MMA h reads this CTA's kMmaN / 2 columns h kMmaN + rank kMmaN / 2 ..
-                    constexpr int kBoxesPerMma = C::kMmaN / 128;
 #pragma unroll
-                    for (int c = 0; c < BN / 128; ++c) {
-                        const uint32_t h = c / kBoxesPerMma;
-                        if (h < h0 || h >= h0 + nh) continue;   // a column slice loads its own MMA's boxes only
-                        tma_load_2d_pair(sb + c * (BK * 128), &map_w, bar,
-                                         (int32_t)(tn * BN + h * C::kMmaN + rank * (C::kMmaN / 2) +
-                                                   (c % kBoxesPerMma) * 64),
-                                         (int32_t)(kb * BK));
+                    for (int q = 0; q < KS; ++q) {
+                        uint8_t *sa = smem + (stage * KS + q) * C::kStageBytes;
+                        uint8_t *sb = sa + C::kABytes;
+                        const int32_t k0 = (int32_t)((kb + q) * BK);
+                        tma_load_2d_pair(sa, &map_x, bar, k0, (int32_t)(tm * 256 + rank * 128));
+                        // 64-column boxes: MMA h reads this CTA's kMmaN / 2 columns h kMmaN + rank kMmaN / 2 ..
+                        constexpr int kBoxesPerMma = C::kMmaN / 128;
+#pragma unroll
+                        for (int c = 0; c < BN / 128; ++c) {
+                            const uint32_t h = c / kBoxesPerMma;
+                            if (h < h0 || h >= h0 + nh) continue;   // a column slice loads its own MMA's boxes only
+                            tma_load_2d_pair(sb + c * (BK * 128), &map_w, bar,
+                                             (int32_t)(tn * BN + h * C::kMmaN + rank * (C::kMmaN / 2) +
+                                                       (c % kBoxesPerMma) * 64),
+                                             k0);
+                        }
                     }
                     if (++stage == S) {
                         stage = 0;
@@ -759,22 +766,25 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                 if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort, a.err)) break;
                 tc_fence_after();
                 const uint32_t d = tmem_base + acc * BN;
-                for (uint32_t kb = 0; kb < a.k_blocks; ++kb) {
+                for (uint32_t kb = 0; kb < a.k_blocks; kb += KS) {
                     if (!mbar_wait(&full[stage], phase, abort, a.err)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint64_t so = (stage * C::kStageBytes) >> 4;
-                    const uint64_t ad = a_desc0 + so, bd = b_desc0 + so;
 #pragma unroll
-                    for (int j = 0; j < BK / 16; ++j)
+                    for (int q = 0; q < KS; ++q) {
+                        const uint64_t so = ((stage * KS + q) * C::kStageBytes) >> 4;
+                        const uint64_t ad = a_desc0 + so, bd = b_desc0 + so;
 #pragma unroll
-                        for (uint32_t h = 0; h < NH; ++h)
-                            if (NH == 1 || (h >= h0 && h < h0 + nh))
-                                umma_f16_ss_pair_if(is0, d + h * C::kMmaN, ad + (uint64_t)(j * 2),
-                                                    bd + (uint64_t)((h * (C::kMmaN / 2) * BK * 2 + j * 2048) >> 4),
-                                                    idesc, (kb > 0 || j > 0) ? 1u : 0u);
+                        for (int j = 0; j < BK / 16; ++j)
+#pragma unroll
+                            for (uint32_t h = 0; h < NH; ++h)
+                                if (NH == 1 || (h >= h0 && h < h0 + nh))
+                                    umma_f16_ss_pair_if(is0, d + h * C::kMmaN, ad + (uint64_t)(j * 2),
+                                                        bd + (uint64_t)((h * (C::kMmaN / 2) * BK * 2 + j * 2048) >> 4),
+                                                        idesc, (kb + q > 0 || j > 0) ? 1u : 0u);
+                    }
                     umma_commit_pair_mask_if(is0, &empty[stage], 0x3);
                     if (++stage == S) {
                         stage = 0;
@@ -1065,13 +1075,13 @@ PairUnits pair_units(uint32_t num_tiles, uint32_t bn, uint32_t sm_pairs) {
     return r;
 }
 
-template <int BN, bool RES = false>
+template <int BN, bool RES = false, int KS = 1>
 int launch_pair(const Plan &p, const CUtensorMap &mx, const CUtensorMap &mw, const CUtensorMap &mz,
                 const CUtensorMap &mr, GemmArgs a, cudaStream_t st) {
     static bool done[sh::kMaxDevices] = {};
     const int d = sh::current_device() % sh::kMaxDevices;
     if (!done[d]) {
-        if (!sh::cuda_ok(cudaFuncSetAttribute(k_gemm_tc2<BN, RES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        if (!sh::cuda_ok(cudaFuncSetAttribute(k_gemm_tc2<BN, RES, KS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                               (int)PairCfg<BN, RES>::kSmem),
                          "cudaFuncSetAttribute(gemm pair)"))
             return -1;
@@ -1084,7 +1094,7 @@ int launch_pair(const Plan &p, const CUtensorMap &mx, const CUtensorMap &mw, con
     a.full_units = pu.full;
     a.num_units = pu.units;
     const uint32_t pairs = min(a.num_units, sm_pairs);
-    return sh::cuda_ok(sh::launch_pdl(k_gemm_tc2<BN, RES>, dim3(2 * pairs), dim3(kPairThreads),
+    return sh::cuda_ok(sh::launch_pdl(k_gemm_tc2<BN, RES, KS>, dim3(2 * pairs), dim3(kPairThreads),
                                       PairCfg<BN, RES>::kSmem, st, mx, mw, mz, mr, a),
                        "sh_gemm launch (pair)")
                ? 0
@@ -1220,7 +1230,14 @@ int gemm_run(uint64_t x, uint64_t w, uint64_t z, uint32_t M, uint32_t N, uint32_
         if (p.pair_bn == 256 && res_tma_env && a.tma_store && (a.flags & SH_EPI_RESIDUAL) &&
             make_map_2d_sw(&mr, (const void *)resid, M, N, ldr, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B))
             return launch_pair<256, true>(p, mx, mw, mz, mr, a, st);
-        return p.pair_bn == 512 ? launch_pair<512>(p, mx, mw, mz, mx, a, st) : launch_pair<256>(p, mx, mw, mz, mx, a, st);
+        if (p.pair_bn == 512) return launch_pair<512>(p, mx, mw, mz, mx, a, st);
+        // an even k-block count: one barrier round trip per two k-steps (SH_GEMM_KS=1 keeps one per k-step)
+        static const bool ks2_env = [] {
+            const char *e = getenv("SH_GEMM_KS");
+            return !(e && atoi(e) == 1);
+        }();
+        if (ks2_env && a.k_blocks % 2 == 0) return launch_pair<256, false, 2>(p, mx, mw, mz, mx, a, st);
+        return launch_pair<256>(p, mx, mw, mz, mx, a, st);
     }
     switch (p.bn) {
         case 256: return launch_tc<256>(p, mx, mw, mz, a, st);
