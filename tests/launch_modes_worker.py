@@ -1,8 +1,9 @@
 """Runs a small encoder forward (2 SigLIP-base layers, B = 12: 2-CTA and 1-CTA GEMMs, tcgen05 attention, LayerNorm),
 one wide GEMM (2816 x 4096 x 256: 11 x 16 pair tiles, a partial tile group) and two long-K GEMMs (4096 x 4096 x
 2048: 256 x 512 pair tiles; 8192 x 4096 x 2048: the same with a tail wave of column slices) on GPU 0 and prints the SHA-1 of their output bytes. tests/test_launch_modes_gpu.py runs it
-under different launch settings (SH_PDL, SH_GEMM_GROUP_M, SH_GEMM_PAIR_BN), which are read once per process, and
-requires identical bytes: the launch mode, the tile order and the tile width must not change any result."""
+under different launch settings (SH_PDL, SH_GEMM_GROUP_M, SH_GEMM_PAIR_BN, SH_GEMM_KS), which are read once per
+process, and requires identical bytes: the launch mode, the tile order, the tile width and the barrier grouping must
+not change any result."""
 from __future__ import annotations
 
 import hashlib

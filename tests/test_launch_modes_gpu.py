@@ -1,6 +1,7 @@
 """Launch settings change timing only: programmatic dependent launch on / off (SH_PDL), the GEMM tile order
-(SH_GEMM_GROUP_M: 1 = row-major, default 8 = grouped) and the pair tile width (SH_GEMM_PAIR_BN: 256 instead of the
-planner's 512 for long K) give bit-identical encoder and GEMM outputs. Each setting is read once per process, so
+(SH_GEMM_GROUP_M: 1 = row-major, default 8 = grouped), the pair tile width (SH_GEMM_PAIR_BN: 256 instead of the
+planner's 512 for long K) and the barrier grouping of the 2-CTA kernel (SH_GEMM_KS=1: one barrier per stage instead
+of one per stage pair) give bit-identical encoder and GEMM outputs. Each setting is read once per process, so
 every variant runs in its own process (tests/launch_modes_worker.py)."""
 from __future__ import annotations
 
@@ -30,3 +31,5 @@ def test_launch_modes_are_bit_identical():
     assert _hashes(SH_GEMM_GROUP_M="1") == base
     assert _hashes(SH_GEMM_GROUP_M="3", SH_PDL="0") == base
     assert _hashes(SH_GEMM_PAIR_BN="256") == base
+    assert _hashes(SH_GEMM_KS="1") == base
+    assert _hashes(SH_GEMM_KS="1", SH_GEMM_PAIR_BN="256") == base
