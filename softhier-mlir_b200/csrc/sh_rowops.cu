@@ -74,6 +74,85 @@ __device__ __forceinline__ float sqdev8(const uint4 &raw, float mean) {
     return q;
 }
 
+// sum over the LPR lanes of a row group (LPR = 32: the warp; 16: each half-warp), every lane taking part
+template <int LPR>
+__device__ __forceinline__ float group_sum(float v) {
+#pragma unroll
+    for (int o = LPR / 2; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// Two rows per warp (LPR = 16 lanes per row) for 528-768 columns: each lane holds six 16-byte vectors of its row, as
+// many bytes as the warp-per-row kernel's three, so 64 rows are in flight per SM instead of 48. Blocks of four warps
+// (8 K registers) fit beside a running GEMM CTA, so with programmatic dependent launch one waits on every SM.
+constexpr uint32_t kHwWarps = 4;
+template <int VPL, bool ADD, int LPR = 16>
+__global__ void __launch_bounds__(kHwWarps * 32, 8)
+    k_layernorm_hw(__half *y, __half *h, const __half *a, const __half *b, const __half *g, const __half *be,
+                    uint32_t rows, uint32_t cols, uint32_t ld, float eps) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const uint32_t lane = threadIdx.x & 31;
+    const uint32_t sub = lane % LPR;
+    const uint32_t row = (blockIdx.x * kHwWarps + (threadIdx.x >> 5)) * (32 / LPR) + lane / LPR;
+    // (a half-warp whose row is past the end still takes part in the shuffles)
+    const bool live = row < rows;
+    const uint32_t cv = cols >> 3;
+    const __half *ar = a + (size_t)row * ld;
+    uint4 x[VPL];
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+        const uint32_t v = sub + LPR * i;
+        x[i] = make_uint4(0u, 0u, 0u, 0u);
+        if (live && v < cv) x[i] = *reinterpret_cast<const uint4 *>(ar + 8 * v);
+    }
+    if (ADD) {   // h = fp16(a + b), stored, and normalised below
+#pragma unroll
+        for (int i = 0; i < VPL; ++i) {
+            const uint32_t v = sub + LPR * i;
+            if (live && v < cv) {
+                const uint4 bb = *reinterpret_cast<const uint4 *>(b + (size_t)row * ld + 8 * v);
+                __half2 *xh = reinterpret_cast<__half2 *>(&x[i]);
+                const __half2 *bh = reinterpret_cast<const __half2 *>(&bb);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const float2 fa = __half22float2(xh[j]), fb = __half22float2(bh[j]);
+                    xh[j] = __floats2half2_rn(fa.x + fb.x, fa.y + fb.y);
+                }
+                *reinterpret_cast<uint4 *>(h + (size_t)row * ld + 8 * v) = x[i];
+            }
+        }
+    }
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) s += sum8(x[i]);   // zero vectors past the row add nothing
+    const float inv_cols = 1.f / (float)cols;
+    const float mean = group_sum<LPR>(s) * inv_cols;
+    float q = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i)
+        if (sub + LPR * i < cv) q += sqdev8(x[i], mean);
+    const float rstd = rsqrtf(group_sum<LPR>(q) * inv_cols + eps);
+    __half *yr = y + (size_t)row * ld;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+        const uint32_t v = sub + LPR * i;
+        if (live && v < cv) {
+            const uint4 gr = *reinterpret_cast<const uint4 *>(g + 8 * v), br = *reinterpret_cast<const uint4 *>(be + 8 * v);
+            const __half2 *xh = reinterpret_cast<const __half2 *>(&x[i]), *gh = reinterpret_cast<const __half2 *>(&gr),
+                          *bh = reinterpret_cast<const __half2 *>(&br);
+            uint4 o;
+            __half2 *oh = reinterpret_cast<__half2 *>(&o);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float2 fx = __half22float2(xh[j]), fg = __half22float2(gh[j]), fb = __half22float2(bh[j]);
+                oh[j] = __floats2half2_rn((fx.x - mean) * rstd * fg.x + fb.x, (fx.y - mean) * rstd * fg.y + fb.y);
+            }
+            *reinterpret_cast<uint4 *>(yr + 8 * v) = o;
+        }
+    }
+}
+
 template <int VPL, bool ADD>
 __global__ void __launch_bounds__(kWarpsPerBlock * 32, VPL <= 4 ? 6 : 1) k_layernorm_vec(__half *y, __half *h, const __half *a,
                                                                           const __half *b, const __half *g,
@@ -512,13 +591,20 @@ void launch_ew(uint64_t y, uint64_t x, uint64_t b, uint32_t rows, uint32_t cols,
     sh::cuda_ok(cudaGetLastError(), name);
 }
 
-template <bool ADD, int VPL>
+template <bool ADD, int VPL, int LPR = 32>
 void ln_vec_launch(uint64_t y, uint64_t h, uint64_t a, uint64_t b, uint64_t g, uint64_t be, uint32_t rows,
                    uint32_t cols, uint32_t ld, float eps, cudaStream_t st) {
-    const uint32_t grid = (rows + kWarpsPerBlock - 1) / kWarpsPerBlock;
-    sh::launch_pdl(k_layernorm_vec<VPL, ADD>, dim3(grid), dim3(kWarpsPerBlock * 32), 0, st, (__half *)y, (__half *)h, (const __half *)a,
-                                                                     (const __half *)b, (const __half *)g,
-                                                                     (const __half *)be, rows, cols, ld, eps);
+    const uint32_t warps = LPR == 32 ? kWarpsPerBlock : kHwWarps;
+    const uint32_t rows_per_block = warps * (32 / LPR);
+    const uint32_t grid = (rows + rows_per_block - 1) / rows_per_block;
+    if constexpr (LPR == 32)
+        sh::launch_pdl(k_layernorm_vec<VPL, ADD>, dim3(grid), dim3(warps * 32), 0, st, (__half *)y,
+                       (__half *)h, (const __half *)a, (const __half *)b, (const __half *)g, (const __half *)be, rows,
+                       cols, ld, eps);
+    else
+        sh::launch_pdl(k_layernorm_hw<VPL, ADD, LPR>, dim3(grid), dim3(warps * 32), 0, st, (__half *)y,
+                       (__half *)h, (const __half *)a, (const __half *)b, (const __half *)g, (const __half *)be, rows,
+                       cols, ld, eps);
 }
 
 template <bool ADD>
@@ -540,6 +626,8 @@ void launch_layernorm(uint64_t y, uint64_t h, uint64_t a, uint64_t b, uint64_t g
                                                          (const __half *)b, (const __half *)g, (const __half *)be, cols, ld, eps)
         if (vpt <= 2) SH_LNR(2); else if (vpt <= 3) SH_LNR(3); else SH_LNR(4);
 #undef SH_LNR
+    } else if (vec && cols > 512 && cols <= 768) {   // two rows per warp, six vectors per lane
+        ln_vec_launch<ADD, 6, 16>(y, h, a, b, g, be, rows, cols, ld, eps, st);
     } else if (vec) {
         const int vpl = (int)((cols / 8 + 31) / 32);
         switch (vpl) {
