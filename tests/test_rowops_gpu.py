@@ -116,6 +116,33 @@ def test_add_layernorm_fused(gpu_lib):
     assert ok, err
 
 
+@pytest.mark.parametrize("rows", [1, 3, 301])
+@pytest.mark.parametrize("cols,ld", [(528, 528), (640, 648), (768, 768), (768, 1024)])
+def test_layernorm_two_rows_per_warp(gpu_lib, rows, cols, ld):
+    """528-768 columns run two rows per warp (16 lanes per row): an odd row count leaves the second half of the last
+    warp past the end (it still takes part in the shuffles), a leading dim above cols leaves a gap between rows that
+    must stay untouched; plain and fused with the residual add."""
+    rt, lib = gpu_lib, gpu_lib.lib
+    rt.reset()
+    a, b = lcg.normal_fp16(rows, ld, 11), lcg.normal_fp16(rows, ld, 12)
+    g, be = lcg.normal_fp16(1, cols, 13, 1.0, 0.1), lcg.normal_fp16(1, cols, 14, 0.0, 0.1)
+    da, db, dg, dbe = (rt.upload(t) for t in (a, b, g, be))
+    sentinel = np.full((rows, ld), 7.0, np.float16)
+    y, h, y2 = rt.upload(sentinel), rt.upload(sentinel), rt.upload(sentinel)
+    lib.sh_layernorm(y, da, dg, dbe, rows, cols, ld, 1e-6, A)
+    lib.sh_cuda_add_layernorm(h, y2, da, db, dg, dbe, rows, cols, ld, 1e-6)
+    rt.check()
+    got, hs, got2 = (rt.get(p, rows, ld) for p in (y, h, y2))
+    ok, err = _tol_ok(got[:, :cols], ops.layernorm(a[:, :cols], g, be, 1e-6))
+    assert ok, err
+    hr = ops.r16(ops.add(a[:, :cols], b[:, :cols]))
+    assert (hs[:, :cols] == hr.astype(np.float16)).all()
+    ok, err = _tol_ok(got2[:, :cols], ops.layernorm(hr, g, be, 1e-6))
+    assert ok, err
+    for t in (got, hs, got2):   # the columns between cols and ld are not written
+        assert (t[:, cols:] == 7.0).all()
+
+
 def test_transpose_ragged_and_strided(gpu_lib):
     rt, lib = gpu_lib, gpu_lib.lib
     rt.reset()
