@@ -6,8 +6,9 @@
 // per SM, or one cluster of two per SM pair) run a warp-specialised tcgen05 pipeline:
 //   warp 0     TMA producer: X tile [128 x 64] (K-major) and W tiles [64 x 64] (N-major, i.e. W as stored) per
 //              stage into a ring of 128-byte-swizzled shared memory, completion on mbarriers;
-//   warp 1     MMA issuer: one thread issues tcgen05.mma into a tensor-memory accumulator; tcgen05.commit frees
-//              each stage and publishes each finished accumulator;
+//   warp 1     MMA issuer: the whole warp walks the issue loop and lane 0 issues tcgen05.mma into a tensor-memory
+//              accumulator; tcgen05.commit frees each stage (in the 2-CTA kernel one commit signals both CTAs) and
+//              publishes each finished accumulator;
 //   warps 2-9  epilogue: tcgen05.ld the accumulator (warp w owns TMEM lane quarter w % 4 = 32 rows, and half of
 //              the columns), apply the fused epilogue (accumulate / bias / GELU / residual / fp32 in or out) and
 //              write fp16 through 32 x 32 staging tiles and TMA stores.
@@ -15,7 +16,8 @@
 //   split-K: fp32 partial tiles in a workspace, the last CTA of a tile (arrival counter) sums them in split order.
 // k_gemm_tc2<BN>: a cluster of two CTAs, tcgen05.mma.cta_group::2 (M = 256), each CTA loading its half of the W
 //   columns; BN = 256 with two accumulators, or BN = 512 (two N = 256 MMAs per k-step, one accumulator, 25 % fewer
-//   operand bytes per MAC) for long K loops, whose short last wave may run as 256-column slices (pair_unit).
+//   operand bytes per MAC) for long K loops, whose short last wave may run as 256-column slices (pair_unit);
+//   KS = 2 (BN = 256 without a residual, even k-block count): stages go in pairs that share one barrier.
 // Tiles are taken in groups of row-tiles (tile_coords) so that concurrent CTAs share X and W in L2, and every launch
 // uses programmatic dependent launch (set-up overlaps the previous kernel). The planner (make_plan, queryable as
 // sh_cuda_gemm_plan) picks the kernel and tiling per shape.
