@@ -249,8 +249,9 @@ int sh_attention_gqa(uint64_t q, uint64_t k, uint64_t v, uint64_t o, uint32_t S,
 // Work item = (sequence b, head h, pair of 128-row query tiles); a CTA per SM walks the items. 320 threads:
 //   warp 0 (one thread)  : TMA loads: the item's two Q tiles into one of two Q slots, K / V blocks of 128 keys into
 //                          a 4-stage ring (separate `full` barriers for K and V, one `empty` barrier per stage);
-//   warp 1 (one thread)  : tcgen05.mma issue. Per key block g: S_t = Q_t K^T (M=128, N=128, K=64) for both tiles t
-//                          into tensor memory as soon as each softmax holds its previous scores, then (one block
+//   warp 1 (lane 0)      : tcgen05.mma issue (the whole warp walks the loop, lane 0 issues). Per key block g:
+//                          S_t = Q_t K^T (M=128, N=128, K=64) for both tiles t into tensor memory as soon as each
+//                          softmax holds its previous scores, then (one block
 //                          behind, so the next scores are ready when a softmax finishes) O_t (+)= P_t V (M=128, N=64,
 //                          K=128; P from tensor memory, V MN-major from shared memory). (One issuer thread per tile measured
 //                          6 % slower at B = 512, S = 256.)
